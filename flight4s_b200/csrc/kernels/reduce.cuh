@@ -1,0 +1,352 @@
+// Full-array reductions over one device buffer: f32 sum (f64 accumulation),
+// i32 sum (two's-complement wrap, bit-exact in any order), and f32 max with
+// lowest-index argmax under IEEE totalOrder.
+//
+// The reference IR has a single reduction node, `ReduceSum`
+// (core/src/main/scala/flight4s/core/ir/IR.scala:96-107), which its code
+// generator lowers to a per-thread serial loop
+// (core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:383-403).
+// These kernels are the parallel lowering of that node (and of the max/argmax
+// the reference lacks) for sm_100a:
+//
+//   1. a grid-stride streaming pass with 128-bit loads, kReduceUnroll vectors
+//      per thread in flight;
+//   2. warp combine (shuffles, or redux.sync for i32) then a CTA combine in
+//      shared memory;
+//   3. a thread-block-cluster combine: every CTA deposits its partial in the
+//      cluster leader's shared memory through DSMEM, so only one partial per
+//      cluster reaches global memory;
+//   4. the last cluster to finish (atomic ticket, nothing waits) folds all
+//      cluster partials in index order and writes the result.  The result is
+//      deterministic for a given grid, and no second kernel is launched.
+//
+// Accumulation follows the reference's `AccumulatorType` rules
+// (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230): I32
+// accumulates in I32 (wrapping); F32 sums are carried in f64 above 32-element
+// fp32 runs, which costs no bandwidth and keeps a 2^32-element sum accurate
+// to ~1e-12 of sum|x|.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace f4s {
+namespace cg = cooperative_groups;
+
+constexpr int kReduceBlock = 512;
+constexpr int kReduceUnroll = 8;
+constexpr int kReduceMaxCluster = 8;
+// Workspace layout: [0,4) ticket counter; cluster partials from byte 256,
+// 16 bytes each.
+constexpr int kReducePartialOffset = 256;
+constexpr int kReducePartialBytes = 16;
+
+struct ArgmaxPartial {
+  int32_t key;    // total_order_key of the value
+  int64_t index;  // INT64_MAX: no candidate
+};
+
+// (key desc, index asc): keep the lexicographic winner.
+__device__ __forceinline__ void argmax_merge(ArgmaxPartial& a, const ArgmaxPartial& b) {
+  if (b.key > a.key || (b.key == a.key && b.index < a.index)) a = b;
+}
+
+// --------------------------------------------------------------- op policies
+// Each policy supplies: the per-thread state, the vector-body step, the
+// scalar head/tail step, the partial type with its identity / merge / warp
+// merge, and how the final partial is written to `out`.
+
+struct SumF32Op {
+  using Partial = double;
+  struct Thread {
+    double acc = 0.0;
+  };
+  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t, uint64_t, int count) {
+    float s[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      s[u] = (u < count) ? (v[u].x + v[u].y) + (v[u].z + v[u].w) : 0.0f;
+    }
+#pragma unroll
+    for (int w = 1; w < kReduceUnroll; w <<= 1) {
+#pragma unroll
+      for (int u = 0; u + w < kReduceUnroll; u += 2 * w) s[u] += s[u + w];
+    }
+    t.acc += static_cast<double>(s[0]);
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t) {
+    t.acc += static_cast<double>(x);
+  }
+  static __device__ __forceinline__ Partial finish(Thread& t, const float*, uint64_t) { return t.acc; }
+  static __device__ __forceinline__ Partial identity() { return 0.0; }
+  static __device__ __forceinline__ Partial merge(Partial a, Partial b) { return a + b; }
+  static __device__ __forceinline__ Partial warp_merge(Partial v) { return warp_sum_f64(v); }
+  static __device__ __forceinline__ Partial load_cg(const Partial* p) { return __ldcg(p); }
+  static __device__ __forceinline__ void write(void* out, Partial r, uint64_t, int accumulate) {
+    double* o = static_cast<double*>(out);
+    *o = accumulate ? *o + r : r;
+  }
+};
+
+struct SumI32Op {
+  using Partial = int32_t;
+  struct Thread {
+    uint32_t acc = 0;
+  };
+  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t, uint64_t, int count) {
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      if (u < count) {
+        t.acc += (__float_as_uint(v[u].x) + __float_as_uint(v[u].y)) +
+                 (__float_as_uint(v[u].z) + __float_as_uint(v[u].w));
+      }
+    }
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t) {
+    t.acc += __float_as_uint(x);
+  }
+  static __device__ __forceinline__ Partial finish(Thread& t, const float*, uint64_t) {
+    return static_cast<int32_t>(t.acc);
+  }
+  static __device__ __forceinline__ Partial identity() { return 0; }
+  static __device__ __forceinline__ Partial merge(Partial a, Partial b) {
+    return static_cast<int32_t>(static_cast<uint32_t>(a) + static_cast<uint32_t>(b));
+  }
+  static __device__ __forceinline__ Partial warp_merge(Partial v) {
+    return static_cast<int32_t>(__reduce_add_sync(0xffffffffu, static_cast<uint32_t>(v)));
+  }
+  static __device__ __forceinline__ Partial load_cg(const Partial* p) { return __ldcg(p); }
+  static __device__ __forceinline__ void write(void* out, Partial r, uint64_t, int accumulate) {
+    int32_t* o = static_cast<int32_t*>(out);
+    *o = accumulate ? merge(*o, r) : r;
+  }
+};
+
+// Output record of the argmax kernel (two 64-bit words):
+//   out[0] = (i64)(order key of the max) << 32 | (0xFFFFFFFF - index): the
+//            packed form whose signed 64-bit max across devices (NCCL
+//            int64 MAX) is again the (max value, lowest index) pair; valid
+//            while index < 2^32; INT64_MIN for an empty input;
+//   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
+struct ArgmaxF32Op {
+  using Partial = ArgmaxPartial;
+  struct Thread {
+    int32_t vkey = INT32_MIN;  // best key seen in the vector body
+    uint64_t best_vec = UINT64_MAX;
+    ArgmaxPartial s{INT32_MIN, INT64_MAX};  // scalar head/tail candidate
+  };
+  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t base,
+                                              uint64_t stride, int count) {
+    // The hot loop tracks only the best vector; the lane inside it is
+    // resolved once at the end.  Vectors arrive in increasing index order,
+    // so a strict '>' keeps the lowest index.
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      if (u < count) {
+        const int32_t k =
+            max(max(total_order_key(v[u].x), total_order_key(v[u].y)),
+                max(total_order_key(v[u].z), total_order_key(v[u].w)));
+        if (k > t.vkey) {
+          t.vkey = k;
+          t.best_vec = base + u * stride;
+        }
+      }
+    }
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t index) {
+    argmax_merge(t.s, ArgmaxPartial{total_order_key(x), static_cast<int64_t>(index)});
+  }
+  static __device__ __forceinline__ Partial finish(Thread& t, const float* in, uint64_t head) {
+    ArgmaxPartial p = t.s;
+    if (t.best_vec != UINT64_MAX) {
+      // One re-read of the winning vector (an L2 hit) finds its lowest lane.
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(in + head) + t.best_vec);
+      int lane = 3;
+      if (total_order_key(v.z) == t.vkey) lane = 2;
+      if (total_order_key(v.y) == t.vkey) lane = 1;
+      if (total_order_key(v.x) == t.vkey) lane = 0;
+      argmax_merge(p, ArgmaxPartial{t.vkey, static_cast<int64_t>(head + 4 * t.best_vec + lane)});
+    }
+    return p;
+  }
+  static __device__ __forceinline__ Partial identity() { return ArgmaxPartial{INT32_MIN, INT64_MAX}; }
+  static __device__ __forceinline__ Partial merge(Partial a, Partial b) {
+    argmax_merge(a, b);
+    return a;
+  }
+  static __device__ __forceinline__ Partial warp_merge(Partial v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ArgmaxPartial other{__shfl_xor_sync(0xffffffffu, v.key, o),
+                          __shfl_xor_sync(0xffffffffu, v.index, o)};
+      argmax_merge(v, other);
+    }
+    return v;
+  }
+  static __device__ __forceinline__ Partial load_cg(const Partial* p) {
+    const longlong2 raw = __ldcg(reinterpret_cast<const longlong2*>(p));
+    return ArgmaxPartial{static_cast<int32_t>(raw.x), static_cast<int64_t>(raw.y)};
+  }
+  static __device__ __forceinline__ void write(void* out, Partial r, uint64_t index_base, int accumulate) {
+    int64_t* o = static_cast<int64_t*>(out);
+    if (r.index != INT64_MAX) r.index += static_cast<int64_t>(index_base);
+    if (accumulate && o[1] >= 0) {
+      argmax_merge(r, ArgmaxPartial{static_cast<int32_t>(o[0] >> 32), o[1]});
+    }
+    if (r.index == INT64_MAX) {
+      o[0] = INT64_MIN;
+      o[1] = -1;
+      return;
+    }
+    const uint32_t low = (r.index <= 0xFFFFFFFFll) ? 0xFFFFFFFFu - static_cast<uint32_t>(r.index) : 0u;
+    o[0] = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(r.key)) << 32) | low);
+    o[1] = r.index;
+  }
+};
+
+// Partials are stored as 16-byte records so one workspace layout serves
+// every op.
+template <class Partial>
+__device__ __forceinline__ void store_partial(unsigned char* slot, const Partial& p) {
+  *reinterpret_cast<Partial*>(slot) = p;
+}
+template <>
+__device__ __forceinline__ void store_partial<ArgmaxPartial>(unsigned char* slot, const ArgmaxPartial& p) {
+  *reinterpret_cast<longlong2*>(slot) = make_longlong2(p.key, p.index);
+}
+
+// --------------------------------------------------------------- the kernel
+template <class Op>
+__device__ __forceinline__ void reduce_full(const float* __restrict__ in, uint64_t n,
+                                            void* __restrict__ out,
+                                            unsigned char* __restrict__ workspace,
+                                            uint64_t index_base, int accumulate) {
+  using Partial = typename Op::Partial;
+  const cg::cluster_group cluster = cg::this_cluster();
+
+  __shared__ Partial warp_partials[kReduceBlock / kWarp];
+  __shared__ Partial cluster_partials[kReduceMaxCluster];
+  __shared__ int is_last;
+
+  const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t nthreads = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+
+  // [0,n) = scalar head up to the first 16-byte boundary, vector body,
+  // scalar tail (< 4 elements each).
+  const uint64_t addr = reinterpret_cast<uint64_t>(in);
+  uint64_t head = ((16u - (addr & 15u)) & 15u) / 4u;
+  if (head > n) head = n;
+  const uint64_t nvec = (n - head) / 4u;
+  const uint64_t tail_begin = head + 4u * nvec;
+
+  typename Op::Thread t;
+  if (tid < head) Op::scalar(t, in[tid], tid);
+  if (tid < n - tail_begin) Op::scalar(t, in[tail_begin + tid], tail_begin + tid);
+
+  const float4* vin = reinterpret_cast<const float4*>(in + head);
+  const uint64_t step = nthreads * kReduceUnroll;
+  uint64_t base = tid;
+  for (; base + (kReduceUnroll - 1) * nthreads < nvec; base += step) {
+    float4 v[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_f4(vin + base + u * nthreads);
+    Op::body(t, v, base, nthreads, kReduceUnroll);
+  }
+  if (base < nvec) {
+    float4 v[kReduceUnroll];
+    int count = 0;
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      if (base + u * nthreads < nvec) {
+        v[u] = ld_stream_f4(vin + base + u * nthreads);
+        count = u + 1;
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    Op::body(t, v, base, nthreads, count);
+  }
+
+  // thread -> warp -> CTA
+  Partial p = Op::warp_merge(Op::finish(t, in, head));
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  if (lane == 0) warp_partials[warp] = p;
+  __syncthreads();
+
+  // CTA -> cluster leader through distributed shared memory
+  const unsigned rank = cluster.block_rank();
+  const unsigned csize = cluster.num_blocks();
+  if (threadIdx.x == 0) {
+    Partial c = warp_partials[0];
+#pragma unroll
+    for (int w = 1; w < kReduceBlock / kWarp; ++w) c = Op::merge(c, warp_partials[w]);
+    *cluster.map_shared_rank(&cluster_partials[rank], 0) = c;
+  }
+  cluster.sync();
+  if (rank != 0) return;
+
+  // cluster leader: publish one partial and take a ticket
+  const unsigned cluster_id = blockIdx.x / csize;
+  const unsigned num_clusters = gridDim.x / csize;
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(workspace);
+  unsigned char* partials = workspace + kReducePartialOffset;
+  if (threadIdx.x == 0) {
+    Partial c = cluster_partials[0];
+    for (unsigned r = 1; r < csize; ++r) c = Op::merge(c, cluster_partials[r]);
+    store_partial(partials + static_cast<size_t>(cluster_id) * kReducePartialBytes, c);
+    __threadfence();
+    is_last = (atomicAdd(ticket, 1u) == num_clusters - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!is_last) return;
+
+  // last cluster: fold every cluster partial in a fixed order
+  __threadfence();
+  Partial acc = Op::identity();
+  for (unsigned i = threadIdx.x; i < num_clusters; i += blockDim.x) {
+    acc = Op::merge(acc, Op::load_cg(reinterpret_cast<const Partial*>(
+                             partials + static_cast<size_t>(i) * kReducePartialBytes)));
+  }
+  acc = Op::warp_merge(acc);
+  if (lane == 0) warp_partials[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Partial r = warp_partials[0];
+#pragma unroll
+    for (int w = 1; w < kReduceBlock / kWarp; ++w) r = Op::merge(r, warp_partials[w]);
+    *ticket = 0u;  // leave the workspace ready for the next launch
+    Op::write(out, r, index_base, accumulate);
+  }
+}
+
+}  // namespace f4s
+
+// Kernel entry points.  Parameters use only launch-ABI descriptor codes
+// 10 (device pointer), 3 (u32) and 2 (i32): (in, n_lo, n_hi, out, workspace,
+// index_base_lo, index_base_hi, accumulate).
+extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
+f4s_reduce_sum_f32(const float* in, uint32_t n_lo, uint32_t n_hi, double* out,
+                   unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
+                   int accumulate) {
+  f4s::reduce_full<f4s::SumF32Op>(in, f4s::join_u64(n_lo, n_hi), out, workspace,
+                                  f4s::join_u64(base_lo, base_hi), accumulate);
+}
+
+extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
+f4s_reduce_sum_i32(const int32_t* in, uint32_t n_lo, uint32_t n_hi, int32_t* out,
+                   unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
+                   int accumulate) {
+  f4s::reduce_full<f4s::SumI32Op>(reinterpret_cast<const float*>(in),
+                                  f4s::join_u64(n_lo, n_hi), out, workspace,
+                                  f4s::join_u64(base_lo, base_hi), accumulate);
+}
+
+extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
+f4s_reduce_argmax_f32(const float* in, uint32_t n_lo, uint32_t n_hi, int64_t* out,
+                      unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
+                      int accumulate) {
+  f4s::reduce_full<f4s::ArgmaxF32Op>(in, f4s::join_u64(n_lo, n_hi), out, workspace,
+                                     f4s::join_u64(base_lo, base_hi), accumulate);
+}

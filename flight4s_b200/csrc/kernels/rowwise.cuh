@@ -1,0 +1,233 @@
+// Row-wise softmax and RMSNorm over bf16 [rows x cols] with fp32 math.
+//
+// The reference has neither op (no exp, rsqrt or row max in its DSL or
+// codegen); its data model fixes the types: bf16 storage accumulates in f32
+// (core/src/main/scala/flight4s/core/types/CudaType.scala:222-224) and f32 ->
+// bf16 stores round to nearest-even (`__float2bfloat16_rn`,
+// core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:518-523).
+//
+//   softmax: y = bf16_rn( exp(x - max) * (1 / sum exp(x - max)) )
+//   rmsnorm: y = bf16_rn( (x * rsqrt(mean(x^2) + eps)) * w )
+//
+// B200 mapping: one 256-thread CTA per row; a row of up to 256*8*VPT bf16
+// lives in registers (VPT 16-byte vectors per thread), so HBM sees exactly
+// one read and one write per element.  Row reductions are warp shuffles plus
+// one shared-memory exchange.  Rows that are not a multiple of 8 elements
+// wide, or too wide for registers, use a looped kernel that re-reads the row
+// (from L2 for realistic widths) with the same arithmetic.
+#pragma once
+
+#include "common.cuh"
+
+namespace f4s {
+
+constexpr int kRowBlock = 256;
+constexpr int kRowWarps = kRowBlock / kWarp;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Block-wide reductions; every thread receives the result.  `scratch` holds
+// kRowWarps floats and must not be reused until after the next barrier.
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  v = warp_max_f32(v);
+  if ((threadIdx.x % kWarp) == 0) scratch[threadIdx.x / kWarp] = v;
+  __syncthreads();
+  float r = scratch[0];
+#pragma unroll
+  for (int w = 1; w < kRowWarps; ++w) r = fmaxf(r, scratch[w]);
+  return r;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  v = warp_sum_f32(v);
+  if ((threadIdx.x % kWarp) == 0) scratch[threadIdx.x / kWarp] = v;
+  __syncthreads();
+  float r = scratch[0];
+#pragma unroll
+  for (int w = 1; w < kRowWarps; ++w) r += scratch[w];
+  return r;
+}
+
+template <int VPT>
+__device__ __forceinline__ void load_row(const uint16_t* row, int nvec, float (&x)[VPT * 8],
+                                         bool (&valid)[VPT]) {
+  uint4 raw[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = threadIdx.x + k * kRowBlock;
+    valid[k] = v < nvec;
+    raw[k] = valid[k] ? ld_stream_u4(reinterpret_cast<const uint4*>(row) + v) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      x[k * 8 + 2 * j] = bf16_lo(w[j]);
+      x[k * 8 + 2 * j + 1] = bf16_hi(w[j]);
+    }
+  }
+}
+
+template <int VPT>
+__device__ __forceinline__ void store_row(uint16_t* row, const float (&y)[VPT * 8],
+                                          const bool (&valid)[VPT]) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    if (valid[k]) {
+      uint4 r;
+      r.x = pack_bf16x2_rn(y[k * 8 + 0], y[k * 8 + 1]);
+      r.y = pack_bf16x2_rn(y[k * 8 + 2], y[k * 8 + 3]);
+      r.z = pack_bf16x2_rn(y[k * 8 + 4], y[k * 8 + 5]);
+      r.w = pack_bf16x2_rn(y[k * 8 + 6], y[k * 8 + 7]);
+      st_stream_u4(reinterpret_cast<uint4*>(row) + threadIdx.x + k * kRowBlock, r);
+    }
+  }
+}
+
+template <int VPT>
+__device__ __forceinline__ void softmax_row_regs(const uint16_t* in, uint16_t* out, int cols,
+                                                 float* red_a, float* red_b) {
+  const int nvec = cols / 8;
+  float x[VPT * 8];
+  bool valid[VPT];
+  load_row<VPT>(in, nvec, x, valid);
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k)
+    if (valid[k])
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, x[k * 8 + j]);
+  m = block_max(m, red_a);
+  const float ms = m * kLog2e;
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float e = valid[k] ? fast_exp2(fmaf(x[k * 8 + j], kLog2e, -ms)) : 0.0f;
+      x[k * 8 + j] = e;
+      s += e;
+    }
+  s = block_sum(s, red_b);
+  const float inv = 1.0f / s;
+#pragma unroll
+  for (int k = 0; k < VPT * 8; ++k) x[k] *= inv;
+  store_row<VPT>(out, x, valid);
+}
+
+template <int VPT>
+__device__ __forceinline__ void rmsnorm_row_regs(const uint16_t* in, const float (&w)[VPT * 8],
+                                                 uint16_t* out, int cols, float eps, float* red) {
+  const int nvec = cols / 8;
+  float x[VPT * 8];
+  bool valid[VPT];
+  load_row<VPT>(in, nvec, x, valid);
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT * 8; ++k) ss = fmaf(x[k], x[k], ss);
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / static_cast<float>(cols) + eps);
+#pragma unroll
+  for (int k = 0; k < VPT * 8; ++k) x[k] = (x[k] * r) * w[k];
+  store_row<VPT>(out, x, valid);
+}
+
+}  // namespace f4s
+
+// (in, out, rows, cols); cols % 8 == 0 and cols <= 2048 * VPT.
+#define F4S_SOFTMAX_REGS(VPT)                                                              \
+  extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)                              \
+      f4s_softmax_rows_bf16_v##VPT(const uint16_t* __restrict__ in,                          \
+                                   uint16_t* __restrict__ out, int rows, int cols) {         \
+    __shared__ float red_a[f4s::kRowWarps];                                                  \
+    __shared__ float red_b[f4s::kRowWarps];                                                  \
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {                                     \
+      f4s::softmax_row_regs<VPT>(in + static_cast<size_t>(r) * cols,                        \
+                                 out + static_cast<size_t>(r) * cols, cols, red_a, red_b);   \
+      __syncthreads();                                                                       \
+    }                                                                                        \
+  }
+F4S_SOFTMAX_REGS(1)
+F4S_SOFTMAX_REGS(2)
+F4S_SOFTMAX_REGS(4)
+F4S_SOFTMAX_REGS(8)
+#undef F4S_SOFTMAX_REGS
+
+// (in, weight, out, rows, cols, eps); cols % 8 == 0 and cols <= 2048 * VPT.
+// The weight slice of each thread is loaded once and stays in registers
+// while the CTA strides over rows.
+#define F4S_RMSNORM_REGS(VPT)                                                                \
+  extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)                                \
+      f4s_rmsnorm_rows_bf16_v##VPT(const uint16_t* __restrict__ in,                            \
+                                   const uint16_t* __restrict__ weight,                        \
+                                   uint16_t* __restrict__ out, int rows, int cols, float eps) { \
+    __shared__ float red[2][f4s::kRowWarps];                                                   \
+    float w[VPT * 8];                                                                          \
+    bool valid[VPT];                                                                           \
+    f4s::load_row<VPT>(weight, cols / 8, w, valid);                                            \
+    int parity = 0;                                                                            \
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {                                       \
+      f4s::rmsnorm_row_regs<VPT>(in + static_cast<size_t>(r) * cols, w,                       \
+                                 out + static_cast<size_t>(r) * cols, cols, eps, red[parity]); \
+      parity ^= 1;                                                                             \
+    }                                                                                          \
+  }
+F4S_RMSNORM_REGS(1)
+F4S_RMSNORM_REGS(2)
+F4S_RMSNORM_REGS(4)
+F4S_RMSNORM_REGS(8)
+#undef F4S_RMSNORM_REGS
+
+// Looped fallbacks for any width: (in, out, rows, cols) and
+// (in, weight, out, rows, cols, eps).  Same arithmetic as above.
+extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)
+f4s_softmax_rows_bf16_any(const uint16_t* __restrict__ in, uint16_t* __restrict__ out,
+                          int rows, int cols) {
+  using namespace f4s;
+  __shared__ float red_a[kRowWarps];
+  __shared__ float red_b[kRowWarps];
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t* x = in + static_cast<size_t>(r) * cols;
+    uint16_t* y = out + static_cast<size_t>(r) * cols;
+    float m = -INFINITY;
+    for (int c = threadIdx.x; c < cols; c += kRowBlock)
+      m = fmaxf(m, __uint_as_float(static_cast<uint32_t>(x[c]) << 16));
+    m = block_max(m, red_a);
+    const float ms = m * kLog2e;
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += kRowBlock)
+      s += fast_exp2(fmaf(__uint_as_float(static_cast<uint32_t>(x[c]) << 16), kLog2e, -ms));
+    s = block_sum(s, red_b);
+    const float inv = 1.0f / s;
+    for (int c = threadIdx.x; c < cols; c += kRowBlock) {
+      const float e = fast_exp2(fmaf(__uint_as_float(static_cast<uint32_t>(x[c]) << 16), kLog2e, -ms));
+      y[c] = static_cast<uint16_t>(pack_bf16x2_rn(e * inv, 0.0f) & 0xFFFFu);
+    }
+    __syncthreads();
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)
+f4s_rmsnorm_rows_bf16_any(const uint16_t* __restrict__ in, const uint16_t* __restrict__ weight,
+                          uint16_t* __restrict__ out, int rows, int cols, float eps) {
+  using namespace f4s;
+  __shared__ float red[2][kRowWarps];
+  int parity = 0;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t* x = in + static_cast<size_t>(r) * cols;
+    uint16_t* y = out + static_cast<size_t>(r) * cols;
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += kRowBlock) {
+      const float v = __uint_as_float(static_cast<uint32_t>(x[c]) << 16);
+      ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, red[parity]);
+    parity ^= 1;
+    const float rs = rsqrtf(ss / static_cast<float>(cols) + eps);
+    for (int c = threadIdx.x; c < cols; c += kRowBlock) {
+      const float v = __uint_as_float(static_cast<uint32_t>(x[c]) << 16);
+      const float wv = __uint_as_float(static_cast<uint32_t>(weight[c]) << 16);
+      y[c] = static_cast<uint16_t>(pack_bf16x2_rn((v * rs) * wv, 0.0f) & 0xFFFFu);
+    }
+  }
+}

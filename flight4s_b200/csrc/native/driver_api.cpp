@@ -1,0 +1,60 @@
+#include "driver_api.hpp"
+
+#include <dlfcn.h>
+
+#include <mutex>
+
+namespace flight4s::cuda {
+namespace {
+
+using GetProcAddress = CUresult (*)(const char*, void**, int, cuuint64_t,
+                                    CUdriverProcAddressQueryResult*);
+
+struct Loaded {
+  DriverApi api;
+  bool ok = false;
+  std::string why;
+};
+
+Loaded load() {
+  Loaded l;
+  void* lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+  if (lib == nullptr) {
+    const char* err = dlerror();
+    l.why = std::string("cannot load libcuda.so.1: ") + (err ? err : "unknown dlopen error");
+    return l;
+  }
+  auto get = reinterpret_cast<GetProcAddress>(dlsym(lib, "cuGetProcAddress_v2"));
+  if (get == nullptr) {
+    l.why = "libcuda.so.1 does not export cuGetProcAddress_v2 (driver older than CUDA 12)";
+    return l;
+  }
+#define F4S_DRIVER_FN(name)                                                                \
+  {                                                                                        \
+    void* fn = nullptr;                                                                    \
+    CUdriverProcAddressQueryResult found{};                                                \
+    if (get(#name, &fn, CUDA_VERSION, CU_GET_PROC_ADDRESS_DEFAULT, &found) != CUDA_SUCCESS || \
+        fn == nullptr) {                                                                   \
+      l.why = std::string("CUDA driver lacks ") + #name;                                   \
+      return l;                                                                            \
+    }                                                                                      \
+    l.api.name = reinterpret_cast<decltype(l.api.name)>(fn);                               \
+  }
+#include "driver_functions.inc"
+#undef F4S_DRIVER_FN
+  l.ok = true;
+  return l;
+}
+
+}  // namespace
+
+const DriverApi* driver_api(std::string* why) {
+  static const Loaded loaded = load();
+  if (!loaded.ok) {
+    if (why) *why = loaded.why;
+    return nullptr;
+  }
+  return &loaded.api;
+}
+
+}  // namespace flight4s::cuda

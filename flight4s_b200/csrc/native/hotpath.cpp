@@ -1,0 +1,433 @@
+#include "hotpath.hpp"
+
+#include <algorithm>
+#include <stdexcept>
+
+#include "cuda_launcher.hpp"
+#include "launch_contract.hpp"
+
+// The sm_100a cubin, embedded at build time (kernel_image.S).
+extern "C" const unsigned char f4s_kernel_image_begin[];
+extern "C" const unsigned char f4s_kernel_image_end[];
+
+namespace flight4s::cuda {
+namespace {
+
+// Launch constants shared with the kernels (csrc/kernels/*.cuh).
+constexpr int kReduceBlock = 512;
+constexpr int kReduceUnroll = 8;
+constexpr std::uint64_t kReducePartialOffset = 256;
+constexpr std::uint64_t kReducePartialBytes = 16;
+constexpr int kBlockSumThreads = 1024;
+constexpr int kBlockSumCluster = 8;
+constexpr std::int64_t kBlockSumElemsPerCluster = 256LL * 256LL;
+constexpr int kAddBlock = 256;
+constexpr int kRowBlock = 256;
+constexpr int kFp8Threads = 256;
+constexpr int kFp8Block = 128;
+
+void check(CUresult r, const char* what) {
+  if (r != CUDA_SUCCESS) {
+    throw std::runtime_error(std::string(what) + " failed with CUDA error " + std::to_string(r));
+  }
+}
+
+void require_ptr(CUdeviceptr p, const char* what) {
+  if (p == 0) throw std::invalid_argument(std::string(what) + " must not be null");
+}
+
+void require_nonnegative(std::int64_t v, const char* what) {
+  if (v < 0) throw std::invalid_argument(std::string(what) + " must not be negative: " + std::to_string(v));
+}
+
+// RAII push of the hotpath's context around one operator call.
+class Current {
+ public:
+  explicit Current(CUcontext c) : scope_(c) {
+    if (scope_.push_result() != CUDA_SUCCESS) result_ = scope_.push_result();
+  }
+  CUresult result() const { return result_; }
+  CUresult finish(CUresult r) {
+    const CUresult pop = scope_.close();
+    return r == CUDA_SUCCESS ? pop : r;
+  }
+
+ private:
+  CurrentContextScope scope_;
+  CUresult result_ = CUDA_SUCCESS;
+};
+
+}  // namespace
+
+Hotpath* Hotpath::open(CUcontext context) {
+  if (context == nullptr) throw std::invalid_argument("CUDA context handle must not be null");
+  const DriverApi& api = require_driver();
+  CurrentContextScope scope(context);
+  check(scope.push_result(), "cuCtxPushCurrent");
+  auto* hp = new Hotpath();
+  hp->context_ = context;
+  try {
+    check(api.cuModuleLoadDataEx(&hp->module_, f4s_kernel_image_begin, 0, nullptr, nullptr),
+          "loading the sm_100a kernel image (cuModuleLoadDataEx)");
+    CUdevice device = 0;
+    check(api.cuCtxGetDevice(&device), "cuCtxGetDevice");
+    check(api.cuDeviceGetAttribute(&hp->sm_count_, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, device),
+          "cuDeviceGetAttribute(MULTIPROCESSOR_COUNT)");
+    auto occupancy = [&](const char* name, int block) {
+      int blocks = 0;
+      check(api.cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, hp->function(name), block, 0),
+            "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+      return std::max(1, blocks);
+    };
+    hp->shape_.add_grid = hp->sm_count_ * occupancy("f4s_vector_add_f32", kAddBlock);
+    hp->shape_.row_ctas_per_sm = occupancy("f4s_softmax_rows_bf16_v4", kRowBlock);
+    hp->shape_.fp8_grid = hp->sm_count_ * occupancy("f4s_fp8_quant_flat", kFp8Threads);
+    hp->shape_.fill_grid = hp->sm_count_ * occupancy("f4s_fill_synthetic", 256);
+    check(hp->set_reduce_cluster(4), "sizing the reduction grid");
+  } catch (...) {
+    if (hp->module_ != nullptr) api.cuModuleUnload(hp->module_);
+    delete hp;
+    throw;
+  }
+  return hp;
+}
+
+Hotpath::~Hotpath() {
+  if (module_ != nullptr) {
+    if (const DriverApi* api = driver_api()) {
+      CurrentContextScope scope(context_);
+      if (scope.push_result() == CUDA_SUCCESS) api->cuModuleUnload(module_);
+    }
+  }
+}
+
+CUfunction Hotpath::function(const std::string& name) const {
+  const DriverApi& api = require_driver();
+  CUfunction fn = nullptr;
+  const CUresult r = api.cuModuleGetFunction(&fn, module_, name.c_str());
+  if (r != CUDA_SUCCESS) throw std::invalid_argument("no kernel named " + name + " in the hot-path module");
+  return fn;
+}
+
+CUresult Hotpath::set_reduce_cluster(int cluster) {
+  if (cluster < 1 || cluster > 8) throw std::invalid_argument("reduction cluster size must be in [1, 8]");
+  const DriverApi& api = require_driver();
+  CurrentContextScope scope(context_);
+  if (scope.push_result() != CUDA_SUCCESS) return scope.push_result();
+  CUlaunchAttribute attr{};
+  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+  attr.value.clusterDim.x = static_cast<unsigned>(cluster);
+  attr.value.clusterDim.y = 1;
+  attr.value.clusterDim.z = 1;
+  CUlaunchConfig config{};
+  config.gridDimX = static_cast<unsigned>(cluster * sm_count_);
+  config.gridDimY = config.gridDimZ = 1;
+  config.blockDimX = kReduceBlock;
+  config.blockDimY = config.blockDimZ = 1;
+  config.attrs = &attr;
+  config.numAttrs = 1;
+  int clusters = 0;
+  for (const char* name : {"f4s_reduce_sum_f32", "f4s_reduce_sum_i32", "f4s_reduce_argmax_f32"}) {
+    int c = 0;
+    const CUresult r = api.cuOccupancyMaxActiveClusters(&c, function(name), &config);
+    if (r != CUDA_SUCCESS) return r;
+    clusters = clusters == 0 ? c : std::min(clusters, c);
+  }
+  if (clusters <= 0) return CUDA_ERROR_INVALID_CLUSTER_SIZE;
+  shape_.reduce_cluster = cluster;
+  shape_.reduce_max_clusters = clusters;
+  return scope.close();
+}
+
+std::uint64_t Hotpath::reduce_workspace_bytes() const {
+  // One partial slot per co-resident CTA bounds every cluster size: at most
+  // 2048 / kReduceBlock CTAs fit on an SM.
+  const std::uint64_t ctas = static_cast<std::uint64_t>(sm_count_) * (2048 / kReduceBlock);
+  return kReducePartialOffset + kReducePartialBytes * ctas;
+}
+
+std::uint64_t Hotpath::block_sum_workspace_bytes(std::int64_t n) {
+  const std::int64_t clusters = std::max<std::int64_t>(1, (n + kBlockSumElemsPerCluster - 1) / kBlockSumElemsPerCluster);
+  return 256 + 4 * static_cast<std::uint64_t>(clusters);
+}
+
+CUresult Hotpath::launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args) {
+  const DriverApi& api = require_driver();
+  CudaLaunchRequest request{
+      context_, fn, stream,
+      LaunchGeometry{grid, 1, 1, block, 1, 1, 0, cluster > 0, cluster > 0 ? cluster : 0,
+                     cluster > 0 ? 1 : 0, cluster > 0 ? 1 : 0},
+      args.layout()};
+  return launch_in_current_context(api, request);
+}
+
+CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                         CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
+                         int accumulate) {
+  if (n > 0) require_ptr(in, "input buffer");
+  require_ptr(out, "output buffer");
+  require_ptr(workspace, "reduction workspace");
+  if (in % 4 != 0) throw std::invalid_argument("input buffer must be 4-byte aligned");
+  if (op == ReduceOp::kArgmaxF32 && out % 8 != 0)
+    throw std::invalid_argument("argmax output must be 8-byte aligned");
+  if (op == ReduceOp::kSumF32 && out % 8 != 0) throw std::invalid_argument("f64 output must be 8-byte aligned");
+  if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
+  const int cluster = shape_.reduce_cluster;
+  // Enough clusters to give each thread >= one unrolled step, at most one wave.
+  const std::uint64_t per_cluster = static_cast<std::uint64_t>(cluster) * kReduceBlock * 4 * kReduceUnroll;
+  const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
+  const int clusters = static_cast<int>(std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters)));
+  const std::uint64_t need = kReducePartialOffset + kReducePartialBytes * static_cast<std::uint64_t>(clusters);
+  if (workspace_bytes < need) {
+    throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
+                                " bytes, need " + std::to_string(need));
+  }
+  const char* name = op == ReduceOp::kSumF32   ? "f4s_reduce_sum_f32"
+                     : op == ReduceOp::kSumI32 ? "f4s_reduce_sum_i32"
+                                               : "f4s_reduce_argmax_f32";
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32)).ptr(out).ptr(workspace)
+      .u32(static_cast<std::uint32_t>(index_base)).u32(static_cast<std::uint32_t>(index_base >> 32))
+      .i32(accumulate ? 1 : 0);
+  return cur.finish(launch(function(name), stream, clusters * cluster, kReduceBlock, cluster, args));
+}
+
+CUresult Hotpath::block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,
+                                CUdeviceptr out, CUdeviceptr workspace, std::uint64_t workspace_bytes) {
+  require_nonnegative(n, "element count");
+  if (n > 0) {
+    require_ptr(in, "input buffer");
+    require_ptr(partials, "partials buffer");
+  }
+  require_ptr(out, "output buffer");
+  require_ptr(workspace, "block-sum workspace");
+  if (in % 4 != 0 || partials % 4 != 0 || out % 4 != 0 || workspace % 16 != 0)
+    throw std::invalid_argument("block-sum buffers must be 4-byte aligned (workspace 16-byte)");
+  if (workspace_bytes < block_sum_workspace_bytes(n))
+    throw std::invalid_argument("block-sum workspace too small: " + std::to_string(workspace_bytes) +
+                                " bytes, need " + std::to_string(block_sum_workspace_bytes(n)));
+  const int clusters = static_cast<int>(std::max<std::int64_t>(1, (static_cast<std::int64_t>(n) + kBlockSumElemsPerCluster - 1) / kBlockSumElemsPerCluster));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).i32(n).ptr(partials).ptr(out).ptr(workspace);
+  return cur.finish(launch(function("f4s_block_reduce_sum_f32"), stream, clusters * kBlockSumCluster,
+                           kBlockSumThreads, kBlockSumCluster, args));
+}
+
+CUresult Hotpath::vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
+                             std::int32_t n) {
+  require_nonnegative(n, "element count");
+  if (n == 0) return CUDA_SUCCESS;
+  require_ptr(a, "left buffer");
+  require_ptr(b, "right buffer");
+  require_ptr(c, "output buffer");
+  const std::uint64_t elem = bf16 ? 2 : 4;
+  if (a % elem != 0 || b % elem != 0 || c % elem != 0)
+    throw std::invalid_argument("vectorAdd buffers must be aligned to their element size");
+  const std::int64_t per_cta = static_cast<std::int64_t>(kAddBlock) * (bf16 ? 8 : 4);
+  const int grid = static_cast<int>(std::min<std::int64_t>(shape_.add_grid, (n + per_cta - 1) / per_cta));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(a).ptr(b).ptr(c).i32(n);
+  return cur.finish(launch(function(bf16 ? "f4s_vector_add_bf16" : "f4s_vector_add_f32"), stream,
+                           std::max(grid, 1), kAddBlock, 0, args));
+}
+
+namespace {
+
+// Register-resident variant for a row width, or "" for the looped kernel.
+int row_vectors_per_thread(std::int32_t cols, std::uint64_t in, std::uint64_t out) {
+  if (cols % 8 != 0 || (in % 16) != 0 || (out % 16) != 0) return 0;
+  const int nvec = cols / 8;
+  for (int vpt : {1, 2, 4, 8}) {
+    if (nvec <= vpt * kRowBlock) return vpt;
+  }
+  return 0;
+}
+
+}  // namespace
+
+CUresult Hotpath::softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out, std::int32_t rows,
+                               std::int32_t cols) {
+  require_nonnegative(rows, "row count");
+  require_nonnegative(cols, "column count");
+  if (rows == 0 || cols == 0) return CUDA_SUCCESS;
+  require_ptr(in, "input buffer");
+  require_ptr(out, "output buffer");
+  if (in % 2 != 0 || out % 2 != 0) throw std::invalid_argument("bf16 buffers must be 2-byte aligned");
+  const int vpt = row_vectors_per_thread(cols, in, out);
+  const std::string name = vpt ? "f4s_softmax_rows_bf16_v" + std::to_string(vpt) : "f4s_softmax_rows_bf16_any";
+  const CUfunction fn = function(name);
+  int per_sm = shape_.row_ctas_per_sm;
+  {
+    int blocks = 0;
+    if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
+      per_sm = blocks;
+  }
+  const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * per_sm * 8));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).ptr(out).i32(rows).i32(cols);
+  return cur.finish(launch(fn, stream, grid, kRowBlock, 0, args));
+}
+
+CUresult Hotpath::rmsnorm_rows(CUstream stream, CUdeviceptr in, CUdeviceptr weight, CUdeviceptr out,
+                               std::int32_t rows, std::int32_t cols, float eps) {
+  require_nonnegative(rows, "row count");
+  require_nonnegative(cols, "column count");
+  if (rows == 0 || cols == 0) return CUDA_SUCCESS;
+  require_ptr(in, "input buffer");
+  require_ptr(weight, "weight buffer");
+  require_ptr(out, "output buffer");
+  if (in % 2 != 0 || out % 2 != 0 || weight % 2 != 0)
+    throw std::invalid_argument("bf16 buffers must be 2-byte aligned");
+  if (!(eps >= 0.0f)) throw std::invalid_argument("eps must be a non-negative number");
+  int vpt = row_vectors_per_thread(cols, in, out);
+  if (weight % 16 != 0) vpt = 0;
+  const std::string name = vpt ? "f4s_rmsnorm_rows_bf16_v" + std::to_string(vpt) : "f4s_rmsnorm_rows_bf16_any";
+  const CUfunction fn = function(name);
+  int per_sm = shape_.row_ctas_per_sm;
+  {
+    int blocks = 0;
+    if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
+      per_sm = blocks;
+  }
+  // Persistent: one wave of CTAs, each keeps its weight slice in registers.
+  const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * per_sm));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).ptr(weight).ptr(out).i32(rows).i32(cols).f32(eps);
+  return cur.finish(launch(fn, stream, grid, kRowBlock, 0, args));
+}
+
+CUresult Hotpath::fp8_quantize(CUstream stream, CUdeviceptr x, CUdeviceptr codes, CUdeviceptr scales,
+                               std::int32_t rows, std::int32_t cols) {
+  require_nonnegative(rows, "row count");
+  require_nonnegative(cols, "column count");
+  if (rows == 0 || cols == 0) return CUDA_SUCCESS;
+  require_ptr(x, "input buffer");
+  require_ptr(codes, "code buffer");
+  require_ptr(scales, "scale buffer");
+  if (x % 2 != 0 || scales % 4 != 0) throw std::invalid_argument("fp8 quantize buffers are misaligned");
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  const std::int64_t total = static_cast<std::int64_t>(rows) * cols;
+  if (cols % kFp8Block == 0 && x % 16 == 0 && codes % 8 == 0 && total / kFp8Block <= INT32_MAX) {
+    const std::int64_t blocks = total / kFp8Block;
+    const std::int64_t ctas = (blocks / 2 + kFp8Threads / 32 - 1) / (kFp8Threads / 32) + 1;
+    ArgumentPack args;
+    args.ptr(x).ptr(codes).ptr(scales).i32(static_cast<std::int32_t>(blocks));
+    return cur.finish(launch(function("f4s_fp8_quant_flat"), stream,
+                             static_cast<int>(std::min<std::int64_t>(shape_.fp8_grid, ctas)), kFp8Threads, 0, args));
+  }
+  ArgumentPack args;
+  args.ptr(x).ptr(codes).ptr(scales).i32(rows).i32(cols);
+  return cur.finish(launch(function("f4s_fp8_quant_rows"), stream, shape_.fp8_grid, kFp8Threads, 0, args));
+}
+
+CUresult Hotpath::fp8_dequantize(CUstream stream, CUdeviceptr codes, CUdeviceptr scales, CUdeviceptr y,
+                                 std::int32_t rows, std::int32_t cols) {
+  require_nonnegative(rows, "row count");
+  require_nonnegative(cols, "column count");
+  if (rows == 0 || cols == 0) return CUDA_SUCCESS;
+  require_ptr(codes, "code buffer");
+  require_ptr(scales, "scale buffer");
+  require_ptr(y, "output buffer");
+  if (y % 2 != 0 || scales % 4 != 0) throw std::invalid_argument("fp8 dequantize buffers are misaligned");
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  const std::int64_t total = static_cast<std::int64_t>(rows) * cols;
+  if (cols % kFp8Block == 0 && codes % 16 == 0 && y % 16 == 0 && total / kFp8Block <= INT32_MAX) {
+    const std::int64_t blocks = total / kFp8Block;
+    const std::int64_t ctas = (blocks / 4 + kFp8Threads / 32 - 1) / (kFp8Threads / 32) + 1;
+    ArgumentPack args;
+    args.ptr(codes).ptr(scales).ptr(y).i32(static_cast<std::int32_t>(blocks));
+    return cur.finish(launch(function("f4s_fp8_dequant_flat"), stream,
+                             static_cast<int>(std::min<std::int64_t>(shape_.fp8_grid, ctas)), kFp8Threads, 0, args));
+  }
+  ArgumentPack args;
+  args.ptr(codes).ptr(scales).ptr(y).i32(rows).i32(cols);
+  return cur.finish(launch(function("f4s_fp8_dequant_rows"), stream, shape_.fp8_grid, kFp8Threads, 0, args));
+}
+
+CUresult Hotpath::fill_synthetic(CUstream stream, CUdeviceptr out, std::uint64_t n, std::uint64_t offset,
+                                 std::uint64_t seed, std::uint32_t stream_id, int kind, float p0, float p1,
+                                 float p2, float p3, std::int32_t ilo, std::int32_t ihi) {
+  if (n == 0) return CUDA_SUCCESS;
+  require_ptr(out, "output buffer");
+  if (kind < 0 || kind > 5) throw std::invalid_argument("unknown synthetic distribution kind");
+  if (kind == 4 && (ilo > ihi)) throw std::invalid_argument("integer range must satisfy lo <= hi");
+  if (kind == 4 && static_cast<std::int64_t>(ihi) - ilo >= 0xFFFFFFFFLL)
+    throw std::invalid_argument("integer range too wide");
+  if (kind == 5 && !(p2 >= 0.0f && p2 < 1.0f)) throw std::invalid_argument("outlier probability must be in [0, 1)");
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(out).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32))
+      .u32(static_cast<std::uint32_t>(offset)).u32(static_cast<std::uint32_t>(offset >> 32))
+      .u32(static_cast<std::uint32_t>(seed)).u32(static_cast<std::uint32_t>(seed >> 32)).u32(stream_id)
+      .i32(kind).f32(p0).f32(p1).f32(p2).f32(p3).i32(ilo).i32(ihi);
+  return cur.finish(launch(function("f4s_fill_synthetic"), stream, shape_.fill_grid, 256, 0, args));
+}
+
+CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+                              CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
+                              std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream) {
+  if (n > 0 && host_in == nullptr) throw std::invalid_argument("host input must not be null");
+  if (host_out == nullptr) throw std::invalid_argument("host output must not be null");
+  require_ptr(staging, "staging buffer");
+  if (staging % 256 != 0) throw std::invalid_argument("staging buffer must be 256-byte aligned");
+  if (copy_stream == nullptr || compute_stream == nullptr || copy_stream == compute_stream)
+    throw std::invalid_argument("reduce_host needs two distinct non-null streams");
+  // staging = [256 B device-side result | buffer 0 | buffer 1]
+  const std::uint64_t half = ((staging_bytes > 256 ? staging_bytes - 256 : 0) / 2) / 256 * 256;
+  if (half < 256) throw std::invalid_argument("staging buffer too small (need >= 768 bytes)");
+  const std::uint64_t chunk = half / 4;  // elements (4-byte types)
+  const CUdeviceptr result = staging;
+  const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
+  const std::uint64_t out_bytes = op == ReduceOp::kSumF32 ? 8 : op == ReduceOp::kSumI32 ? 4 : 16;
+
+  const DriverApi& api = require_driver();
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  CUevent copied[2] = {nullptr, nullptr};
+  CUevent consumed[2] = {nullptr, nullptr};
+  CUresult r = CUDA_SUCCESS;
+  for (int i = 0; i < 2 && r == CUDA_SUCCESS; ++i) {
+    r = api.cuEventCreate(&copied[i], CU_EVENT_DISABLE_TIMING);
+    if (r == CUDA_SUCCESS) r = api.cuEventCreate(&consumed[i], CU_EVENT_DISABLE_TIMING);
+  }
+  const std::uint64_t chunks = n == 0 ? 1 : (n + chunk - 1) / chunk;
+  for (std::uint64_t k = 0; k < chunks && r == CUDA_SUCCESS; ++k) {
+    const int b = static_cast<int>(k % 2);
+    const std::uint64_t first = k * chunk;
+    const std::uint64_t count = n == 0 ? 0 : std::min(chunk, n - first);
+    if (k >= 2) r = api.cuStreamWaitEvent(copy_stream, consumed[b], 0);
+    if (r == CUDA_SUCCESS && count > 0)
+      r = api.cuMemcpyHtoDAsync(buffers[b], static_cast<const unsigned char*>(host_in) + first * 4, count * 4,
+                                copy_stream);
+    if (r == CUDA_SUCCESS) r = api.cuEventRecord(copied[b], copy_stream);
+    if (r == CUDA_SUCCESS) r = api.cuStreamWaitEvent(compute_stream, copied[b], 0);
+    if (r == CUDA_SUCCESS) {
+      // Pushing the same context again inside reduce() is harmless.
+      r = reduce(op, compute_stream, buffers[b], count, result, workspace, workspace_bytes, first, k > 0 ? 1 : 0);
+    }
+    if (r == CUDA_SUCCESS) r = api.cuEventRecord(consumed[b], compute_stream);
+  }
+  if (r == CUDA_SUCCESS) r = api.cuMemcpyDtoHAsync(host_out, result, out_bytes, compute_stream);
+  if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(compute_stream);
+  if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(copy_stream);
+  for (int i = 0; i < 2; ++i) {
+    if (copied[i]) api.cuEventDestroy(copied[i]);
+    if (consumed[i]) api.cuEventDestroy(consumed[i]);
+  }
+  return cur.finish(r);
+}
+
+}  // namespace flight4s::cuda

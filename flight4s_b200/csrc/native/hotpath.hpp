@@ -1,0 +1,91 @@
+// Hot-path operators: the B200 lowering targets of the reference's
+// reduction node and of the elementwise / row-wise / FP8 kernels.
+//
+// A Hotpath binds one CUDA context to the embedded sm_100a module (loaded
+// with cuModuleLoadDataEx, as the reference loads its generated modules,
+// native/src/cuda_driver.cpp:209-261) and to launch shapes sized for the
+// device (SM count x resident CTAs, cluster occupancy).  Every operator
+// packs its kernel arguments with the reference's descriptor codes and goes
+// through the same cuLaunchKernelEx launcher as user kernels
+// (native/src/cuda_launcher.cpp:8-62).  Operators are asynchronous on the
+// given stream and never allocate: device buffers, including the small
+// reduction workspace, belong to the caller.
+#pragma once
+
+#include <cuda.h>
+
+#include <cstdint>
+#include <string>
+
+#include "cuda_driver.hpp"
+#include "launch_contract.hpp"
+
+namespace flight4s::cuda {
+
+enum class ReduceOp : int { kSumF32 = 0, kSumI32 = 1, kArgmaxF32 = 2 };
+
+struct HotpathShape {
+  int reduce_cluster = 4;       // CTAs per cluster in the full-array reductions
+  int reduce_max_clusters = 0;  // co-resident clusters (occupancy query)
+  int add_grid = 0;
+  int row_ctas_per_sm = 0;
+  int fp8_grid = 0;
+  int fill_grid = 0;
+};
+
+class Hotpath {
+ public:
+  // Loads the module into `context` and sizes launch shapes.
+  static Hotpath* open(CUcontext context);
+  ~Hotpath();
+
+  CUcontext context() const { return context_; }
+  CUmodule module() const { return module_; }
+  int sm_count() const { return sm_count_; }
+  const HotpathShape& shape() const { return shape_; }
+  // Re-size the full-array reduction grid for a cluster size in [1, 8].
+  CUresult set_reduce_cluster(int cluster);
+
+  std::uint64_t reduce_workspace_bytes() const;
+  static std::uint64_t block_sum_workspace_bytes(std::int64_t n);
+
+  CUresult reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                  CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
+                  int accumulate);
+  CUresult block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,
+                         CUdeviceptr out, CUdeviceptr workspace, std::uint64_t workspace_bytes);
+  CUresult vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
+                      std::int32_t n);
+  CUresult softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out, std::int32_t rows,
+                        std::int32_t cols);
+  CUresult rmsnorm_rows(CUstream stream, CUdeviceptr in, CUdeviceptr weight, CUdeviceptr out,
+                        std::int32_t rows, std::int32_t cols, float eps);
+  CUresult fp8_quantize(CUstream stream, CUdeviceptr x, CUdeviceptr codes, CUdeviceptr scales,
+                        std::int32_t rows, std::int32_t cols);
+  CUresult fp8_dequantize(CUstream stream, CUdeviceptr codes, CUdeviceptr scales, CUdeviceptr y,
+                          std::int32_t rows, std::int32_t cols);
+  CUresult fill_synthetic(CUstream stream, CUdeviceptr out, std::uint64_t n, std::uint64_t offset,
+                          std::uint64_t seed, std::uint32_t stream_id, int kind, float p0, float p1,
+                          float p2, float p3, std::int32_t ilo, std::int32_t ihi);
+
+  // End-to-end reduction of a HOST buffer: chunked host->device copies on
+  // `copy_stream` overlapped with per-chunk reductions on `compute_stream`
+  // (double-buffered in `staging`), result copied back to `host_out`, and
+  // both streams synchronized before returning.
+  CUresult reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+                       CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
+                       std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream);
+
+  CUfunction function(const std::string& name) const;
+
+ private:
+  Hotpath() = default;
+  CUresult launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args);
+
+  CUcontext context_ = nullptr;
+  CUmodule module_ = nullptr;
+  int sm_count_ = 0;
+  HotpathShape shape_;
+};
+
+}  // namespace flight4s::cuda

@@ -1,0 +1,188 @@
+"""Hot-path operators on a CudaContext (the sm_100a kernels behind the
+reference's `ReduceSum` node, its vectorAdd / blockReduceSum kernels, and
+the row-wise and FP8 ops).  Declarations and reference citations:
+include/flight4s_b200.h.
+
+Inputs and outputs may be CudaDeviceBuffers, torch CUDA tensors or raw
+device addresses; streams may be CudaStreams, torch.cuda.Streams, raw
+handles or None (the legacy default stream).  `*_into` methods are
+asynchronous; the plain methods synchronize and return host values.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Any, Optional
+
+import numpy as np
+
+from ._native import check, lib
+from .runtime import CudaContext, CudaModule, device_address, stream_handle
+
+REDUCE_SUM_F32, REDUCE_SUM_I32, REDUCE_ARGMAX_F32 = 0, 1, 2
+
+# Synthetic distributions of f4s_fill_synthetic
+UNIFORM_F32, UNIFORM_BF16, NORMAL_F32, NORMAL_BF16, UNIFORM_I32, NORMAL_BF16_OUTLIERS = range(6)
+
+
+def _count(x: Any, n: Optional[int]) -> int:
+    if n is not None:
+        return int(n)
+    if hasattr(x, "element_count"):
+        return int(x.element_count)
+    if hasattr(x, "numel"):
+        return int(x.numel())
+    raise ValueError("element count required for a raw device address")
+
+
+def unpack_argmax_key(packed: int) -> tuple[float, int]:
+    """(value, index) of a packed argmax key:
+    (signed totalOrder key << 32) | (0xFFFFFFFF - index)."""
+    key = packed >> 32                      # arithmetic: signed 32-bit key
+    bits = key ^ ((key >> 31) & 0x7FFFFFFF)
+    value = float(np.array([bits & 0xFFFFFFFF], np.uint32).view(np.float32)[0])
+    return value, 0xFFFFFFFF - (packed & 0xFFFFFFFF)
+
+
+class Hotpath:
+    def __init__(self, context: CudaContext):
+        self.context = context
+        h = C.c_void_p()
+        check(lib.f4s_hotpath_open(context.handle, C.byref(h)), "hot-path module load")
+        self._h = h
+        self.sm_count = lib.f4s_hotpath_sm_count(h)
+        self.module = CudaModule(context, lib.f4s_hotpath_module(h), owned=False)
+        self.workspace_bytes = int(lib.f4s_reduce_workspace_bytes(h))
+        self._workspace = None
+        self._result = None
+
+    # ------------------------------------------------------------ plumbing
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    def workspace(self):
+        """Zeroed reduction workspace owned by this hotpath (one per hotpath:
+        reductions issued on different streams concurrently need their own,
+        allocated with `new_workspace`)."""
+        if self._workspace is None:
+            self._workspace = self.new_workspace()
+        return self._workspace
+
+    def new_workspace(self):
+        ws = self.context.allocate("u8", self.workspace_bytes)
+        ws.copy_from(np.zeros(self.workspace_bytes, np.uint8))
+        return ws
+
+    def _result_buffer(self):
+        if self._result is None:
+            self._result = self.context.allocate("u64", 2)
+        return self._result
+
+    def set_reduce_cluster(self, cluster: int) -> None:
+        check(lib.f4s_hotpath_set_reduce_cluster(self._h, cluster), "reduction cluster size")
+
+    def close(self) -> None:
+        if self._h is not None:
+            for b in (self._workspace, self._result):
+                if b is not None:
+                    b.close()
+            check(lib.f4s_hotpath_close(self._h), "hot-path module unload")
+            self._h = None
+
+    # ------------------------------------------------- full-array reductions
+    def reduce_into(self, op: int, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
+                    accumulate: bool = False, index_base: int = 0, workspace: Any = None) -> None:
+        ws = self.workspace() if workspace is None else workspace
+        ws_bytes = ws.size_bytes if hasattr(ws, "size_bytes") else self.workspace_bytes
+        args = (self._h, stream_handle(stream), device_address(x), _count(x, n), device_address(out),
+                device_address(ws), ws_bytes)
+        if op == REDUCE_SUM_F32:
+            check(lib.f4s_reduce_sum_f32(*args, int(accumulate)), "reduce_sum_f32")
+        elif op == REDUCE_SUM_I32:
+            check(lib.f4s_reduce_sum_i32(*args, int(accumulate)), "reduce_sum_i32")
+        elif op == REDUCE_ARGMAX_F32:
+            check(lib.f4s_reduce_argmax_f32(*args, index_base, int(accumulate)), "reduce_argmax_f32")
+        else:
+            raise ValueError(f"unknown reduction op {op}")
+
+    def _reduce_sync(self, op: int, x: Any, n: Optional[int], stream: Any) -> np.ndarray:
+        out = self._result_buffer()
+        self.reduce_into(op, x, out, n=n, stream=stream)
+        if stream is not None and hasattr(stream, "synchronize"):
+            stream.synchronize()
+        self.context.synchronize()
+        return out.copy_to_array()
+
+    def reduce_sum_f32(self, x: Any, n: Optional[int] = None, stream: Any = None) -> float:
+        return float(self._reduce_sync(REDUCE_SUM_F32, x, n, stream).view(np.float64)[0])
+
+    def reduce_sum_i32(self, x: Any, n: Optional[int] = None, stream: Any = None) -> int:
+        return int(self._reduce_sync(REDUCE_SUM_I32, x, n, stream).view(np.int32)[0])
+
+    def reduce_argmax_f32(self, x: Any, n: Optional[int] = None, stream: Any = None) -> tuple[float, int]:
+        """(max value, index of its first occurrence); (nan, -1) when empty."""
+        r = self._reduce_sync(REDUCE_ARGMAX_F32, x, n, stream).view(np.int64)
+        index = int(r[1])
+        if index < 0:
+            return float("nan"), -1
+        return unpack_argmax_key(int(r[0]))[0], index
+
+    def reduce_host(self, op: int, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
+                    workspace: Any = None) -> np.ndarray:
+        """End-to-end reduction of a host array (pinned for overlap) through
+        `staging` device memory; returns the raw 8/4/16-byte result."""
+        ws = self.workspace() if workspace is None else workspace
+        out = np.zeros(2, np.uint64)
+        host = np.ascontiguousarray(host)
+        check(lib.f4s_reduce_host(self._h, op, host.ctypes.data, host.size, out.ctypes.data,
+                                  device_address(staging), staging.size_bytes, device_address(ws), ws.size_bytes,
+                                  stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")
+        return out
+
+    # ------------------------------------------------------------ block sum
+    @staticmethod
+    def block_reduce_workspace_bytes(n: int) -> int:
+        return int(lib.f4s_block_reduce_workspace_bytes(n))
+
+    def block_reduce_sum_f32_into(self, x: Any, partials: Any, out: Any, workspace: Any, n: Optional[int] = None,
+                                  stream: Any = None) -> None:
+        check(lib.f4s_block_reduce_sum_f32(self._h, stream_handle(stream), device_address(x), _count(x, n),
+                                           device_address(partials), device_address(out),
+                                           device_address(workspace), workspace.size_bytes),
+              "block_reduce_sum_f32")
+
+    # ---------------------------------------------------------- elementwise
+    def vector_add_f32(self, a: Any, b: Any, c: Any, n: Optional[int] = None, stream: Any = None) -> None:
+        check(lib.f4s_vector_add_f32(self._h, stream_handle(stream), device_address(a), device_address(b),
+                                     device_address(c), _count(a, n)), "vectorAdd f32")
+
+    def vector_add_bf16(self, a: Any, b: Any, c: Any, n: Optional[int] = None, stream: Any = None) -> None:
+        check(lib.f4s_vector_add_bf16(self._h, stream_handle(stream), device_address(a), device_address(b),
+                                      device_address(c), _count(a, n)), "vectorAdd bf16")
+
+    # ------------------------------------------------------------- row-wise
+    def softmax_rows_bf16(self, x: Any, y: Any, rows: int, cols: int, stream: Any = None) -> None:
+        check(lib.f4s_softmax_rows_bf16(self._h, stream_handle(stream), device_address(x), device_address(y),
+                                        rows, cols), "softmax rows bf16")
+
+    def rmsnorm_rows_bf16(self, x: Any, w: Any, y: Any, rows: int, cols: int, eps: float = 1e-6,
+                          stream: Any = None) -> None:
+        check(lib.f4s_rmsnorm_rows_bf16(self._h, stream_handle(stream), device_address(x), device_address(w),
+                                        device_address(y), rows, cols, eps), "rmsnorm rows bf16")
+
+    # ------------------------------------------------------------------ fp8
+    def fp8_quantize_e4m3(self, x: Any, codes: Any, scales: Any, rows: int, cols: int, stream: Any = None) -> None:
+        check(lib.f4s_fp8_quantize_e4m3(self._h, stream_handle(stream), device_address(x), device_address(codes),
+                                        device_address(scales), rows, cols), "fp8 e4m3 quantize")
+
+    def fp8_dequantize_e4m3(self, codes: Any, scales: Any, y: Any, rows: int, cols: int, stream: Any = None) -> None:
+        check(lib.f4s_fp8_dequantize_e4m3(self._h, stream_handle(stream), device_address(codes),
+                                          device_address(scales), device_address(y), rows, cols),
+              "fp8 e4m3 dequantize")
+
+    # ------------------------------------------------------------ synthetic
+    def fill_synthetic(self, out: Any, n: int, kind: int, seed: int, offset: int = 0, stream_id: int = 0,
+                       p0: float = 0.0, p1: float = 1.0, p2: float = 0.0, p3: float = 1.0, ilo: int = 0,
+                       ihi: int = 0, stream: Any = None) -> None:
+        check(lib.f4s_fill_synthetic(self._h, stream_handle(stream), device_address(out), n, offset, seed, stream_id,
+                                     kind, p0, p1, p2, p3, ilo, ihi), "synthetic fill")

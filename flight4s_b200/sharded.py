@@ -1,0 +1,126 @@
+"""Full-array reductions sharded over the GPUs of one node.
+
+One process per GPU.  Each rank holds a contiguous shard [offset, offset +
+n_local) of the logical array, reduces it with one kernel launch into a
+small partial, and the partials are combined by one collective:
+
+    sum f32   -> f64 partial,                      all_reduce SUM
+    sum i32   -> i32 partial (two's-complement),   all_reduce SUM (wraps: bit-exact)
+    argmax    -> packed i64 key (signed totalOrder key << 32 | 0xFFFFFFFF - global index),
+                                                    all_reduce MAX
+
+The partial kernels are the hot-path reductions; the collective is
+torch.distributed (NCCL over NVLink on GPUs; gloo in the CPU tests, where
+`partial_fn` supplies the per-rank partial instead of a kernel).
+"""
+from __future__ import annotations
+
+from typing import Any, Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from .hotpath import REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32, unpack_argmax_key
+
+MAX_PACKED_INDEX = 0xFFFFFFFF  # packed argmax keys carry 32-bit global indices
+
+
+def shard_bounds(n_total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous shard of rank `rank`: [offset, offset + count).  The first
+    n_total % world ranks take one extra element."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    base, extra = divmod(n_total, world)
+    offset = rank * base + min(rank, extra)
+    return offset, base + (1 if rank < extra else 0)
+
+
+def combine_sum_f64(partial: torch.Tensor, group: Any = None) -> torch.Tensor:
+    dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
+    return partial
+
+
+def combine_sum_i32(partial: torch.Tensor, group: Any = None) -> torch.Tensor:
+    dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
+    return partial
+
+
+def combine_argmax(packed: torch.Tensor, group: Any = None) -> torch.Tensor:
+    dist.all_reduce(packed, op=dist.ReduceOp.MAX, group=group)
+    return packed
+
+
+class ShardedReducer:
+    """Per-rank reduction + one all_reduce.  Buffers are device tensors
+    allocated once; `*_async` methods only enqueue work on `stream`."""
+
+    def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None):
+        self.hp = hotpath
+        self.device = device
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n_total = n_total
+        self.offset, self.count = shard_bounds(n_total, self.world, self.rank)
+        self.f64 = torch.zeros(1, dtype=torch.float64, device=device)
+        self.i32 = torch.zeros(1, dtype=torch.int32, device=device)
+        self.arg = torch.zeros(2, dtype=torch.int64, device=device)
+        self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
+
+    def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
+        if shard.numel() != self.count:
+            raise ValueError(f"rank {self.rank} shard holds {shard.numel()} elements, expected {self.count}")
+        self.hp.reduce_into(op, shard, out, n=self.count, stream=stream, index_base=self.offset,
+                            workspace=_Workspace(self.workspace))
+
+    def sum_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
+        self._reduce(REDUCE_SUM_F32, shard, self.f64, stream)
+        if self.world > 1:
+            combine_sum_f64(self.f64, self.group)
+        return self.f64
+
+    def sum_i32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
+        self._reduce(REDUCE_SUM_I32, shard, self.i32, stream)
+        if self.world > 1:
+            combine_sum_i32(self.i32, self.group)
+        return self.i32
+
+    def argmax_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
+        if self.n_total - 1 > MAX_PACKED_INDEX:
+            raise ValueError("sharded argmax packs 32-bit global indices: n_total must be <= 2^32")
+        self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
+        if self.world > 1:
+            combine_argmax(self.arg[:1], self.group)
+        return self.arg
+
+    @staticmethod
+    def argmax_result(arg: torch.Tensor) -> tuple[float, int]:
+        packed = int(arg[0].item())
+        if packed == -(1 << 63):
+            return float("nan"), -1
+        return unpack_argmax_key(packed)
+
+
+class _Workspace:
+    """Adapter: a torch uint8 tensor used as the reduction workspace."""
+
+    def __init__(self, t: torch.Tensor):
+        self.t = t
+        self.size_bytes = t.numel()
+
+    def data_ptr(self) -> int:
+        return self.t.data_ptr()
+
+
+def cpu_sharded_combine(partial_fn: Callable[[int, int, int], tuple[float, int, int]], n_total: int) -> tuple:
+    """The combine steps of ShardedReducer on CPU tensors (gloo): `partial_fn
+    (rank, offset, count)` returns this rank's (f64 sum, i32 sum, packed
+    argmax key); returns the combined triple.  Used by the multi-process CPU
+    tests of the collective logic."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    offset, count = shard_bounds(n_total, world, rank)
+    s, i, k = partial_fn(rank, offset, count)
+    ts = combine_sum_f64(torch.tensor([s], dtype=torch.float64))
+    ti = combine_sum_i32(torch.tensor([i], dtype=torch.int32))
+    tk = combine_argmax(torch.tensor([k], dtype=torch.int64))
+    return float(ts.item()), int(ti.item()), int(tk.item())

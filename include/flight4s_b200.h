@@ -1,0 +1,289 @@
+/*
+ * flight4s_b200 — C ABI of the B200 (sm_100a) hot path.
+ *
+ * Two groups of entry points:
+ *
+ *  1. The runtime boundary.  One plain-C function per native method the
+ *     reference's JVM runtime binds (runtime/src/main/java/flight4s/runtime/
+ *     cuda/internal/CudaNativeBindings.java:21-151, implemented in
+ *     native/src/jni_cuda_launcher.cpp and native/src/jni_cuda_driver.cpp).
+ *     Handles travel as uint64_t exactly as the JNI layer passes them as
+ *     `long`; byte arrays and direct buffers become pointer + size.
+ *
+ *  2. The hot-path operators: the sm_100a kernels that replace the
+ *     reference's serial `ReduceSum` lowering
+ *     (core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:383-403),
+ *     its `vectorAdd` / `blockReduceSum` test kernels
+ *     (runtime/src/test/scala/flight4s/runtime/cuda/CudaResourcesJniSuite.scala:108-312)
+ *     and the row-wise / FP8 ops.  They run on an `f4s_hotpath`, which holds
+ *     the embedded sm_100a module loaded into one context.  The kernels are
+ *     also ordinary module functions: f4s_hotpath_module() + f4s_resolve_function()
+ *     + f4s_launch_kernel() launch them through the same descriptor-coded
+ *     path as any user kernel.
+ *
+ * Status convention (every function returning int):
+ *     0                           success
+ *     > 0                         a CUresult from the CUDA driver
+ *     F4S_STATUS_INVALID_ARGUMENT the request was rejected before reaching
+ *                                 the driver (the reference throws
+ *                                 std::invalid_argument -> IllegalArgumentException)
+ *     F4S_STATUS_OVERFLOW         a size or offset overflowed (std::overflow_error)
+ *     F4S_STATUS_DRIVER_UNAVAILABLE libcuda.so.1 could not be loaded
+ *     F4S_STATUS_INTERNAL         any other native failure
+ * The calling thread's last status (name, description, and the module-load
+ * JIT logs the reference returns in NativeCudaDriverResult) is available
+ * from f4s_last_status_*() until the thread's next call.
+ *
+ * Nothing here synchronizes unless its comment says so.
+ */
+#ifndef FLIGHT4S_B200_H_
+#define FLIGHT4S_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define F4S_STATUS_SUCCESS 0
+#define F4S_STATUS_INVALID_ARGUMENT (-1)
+#define F4S_STATUS_OVERFLOW (-2)
+#define F4S_STATUS_DRIVER_UNAVAILABLE (-3)
+#define F4S_STATUS_INTERNAL (-4)
+
+/* ------------------------------------------------------------- diagnostics */
+
+/* ABI version of this header (major * 1000 + minor). */
+int f4s_abi_version(void);
+
+/* Last status of the calling thread: code, CUDA name (e.g. "CUDA_SUCCESS",
+ * "CUDA_ERROR_INVALID_VALUE") or exception text, description, JIT logs.
+ * Fields of NativeCudaDriverResult (NativeCudaDriverResult.java). */
+int f4s_last_status_code(void);
+const char* f4s_last_status_name(void);
+const char* f4s_last_status_description(void);
+const char* f4s_last_info_log(void);
+const char* f4s_last_error_log(void);
+
+/* 1 when libcuda.so.1 loads on this host, else 0 (and the reason in
+ * f4s_last_status_description()).  Never touches a device. */
+int f4s_driver_available(void);
+
+/* ------------------------------------------------------- launch contract */
+
+/* Launch geometry and argument layout checks of the reference's contract
+ * (native/include/flight4s/cuda/launch_contract.hpp:35-42,
+ * native/src/launch_contract.cpp:49-199).  Return 0 when valid, else
+ * F4S_STATUS_INVALID_ARGUMENT with the reference's message in
+ * f4s_last_status_description().  Pure host code: no driver needed. */
+int f4s_validate_launch_geometry(int32_t grid_x, int32_t grid_y, int32_t grid_z, int32_t block_x,
+                                 int32_t block_y, int32_t block_z, int32_t dynamic_shared_memory_bytes,
+                                 int32_t uses_cluster, int32_t cluster_x, int32_t cluster_y,
+                                 int32_t cluster_z);
+int f4s_validate_argument_layout(const void* storage, int64_t storage_size_bytes, const int32_t* offsets,
+                                 size_t offset_count, const int8_t* descriptor_codes,
+                                 size_t descriptor_count);
+
+/* Replaces CudaNativeBindings.launchKernel (CudaNativeBindings.java:21-38;
+ * native/src/jni_cuda_launcher.cpp:155-203 -> CudaLauncher::launch,
+ * native/src/cuda_launcher.cpp:8-62).  `argument_storage` holds the packed
+ * arguments at `argument_offsets` with `argument_descriptor_codes`
+ * (bool 1, i32 2, u32 3, f16 4, bf16 5, f32 6, f64 7, e4m3 8, e5m2 9,
+ * device pointer 10).  Pushes `context`, calls cuLaunchKernelEx (with the
+ * cluster attribute when uses_cluster != 0), restores the caller's context. */
+int f4s_launch_kernel(uint64_t context, uint64_t function, uint64_t stream, int32_t grid_x,
+                      int32_t grid_y, int32_t grid_z, int32_t block_x, int32_t block_y, int32_t block_z,
+                      int32_t dynamic_shared_memory_bytes, int32_t uses_cluster, int32_t cluster_x,
+                      int32_t cluster_y, int32_t cluster_z, void* argument_storage,
+                      int64_t argument_storage_size_bytes, const int32_t* argument_offsets,
+                      const int8_t* argument_descriptor_codes, size_t argument_count);
+
+/* ------------------------------------------------------------- contexts */
+
+/* Replaces retainPrimaryContext (CudaNativeBindings.java:47-48;
+ * native/src/jni_cuda_driver.cpp:427; native/src/cuda_driver.cpp:137-182). */
+int f4s_retain_primary_context(int32_t device_ordinal, uint64_t* context, int32_t* compute_capability_major,
+                               int32_t* compute_capability_minor);
+/* Replaces releasePrimaryContext (CudaNativeBindings.java:50-51; native/src/jni_cuda_driver.cpp:446). */
+int f4s_release_primary_context(int32_t device_ordinal);
+/* Replaces synchronizeContext (CudaNativeBindings.java:53-54; native/src/jni_cuda_driver.cpp:465).  Synchronizes. */
+int f4s_synchronize_context(uint64_t context);
+/* Addition: cuDeviceGetAttribute for the context's device. */
+int f4s_device_attribute(uint64_t context, int32_t attribute, int32_t* value);
+
+/* -------------------------------------------------------------- modules */
+
+/* Replaces loadPtx (CudaNativeBindings.java:56-58; native/src/jni_cuda_driver.cpp:484;
+ * native/src/cuda_driver.cpp:209-261):
+ * NUL-free PTX text, JIT logs in f4s_last_info_log()/f4s_last_error_log(). */
+int f4s_load_ptx(uint64_t context, const uint8_t* ptx, size_t ptx_size, uint64_t* module);
+/* Addition: load a cubin or fatbin image (the PTX path rejects NUL bytes,
+ * native/src/cuda_driver.cpp:214-216, so it cannot carry sm_100a binaries). */
+int f4s_load_module_image(uint64_t context, const void* image, size_t image_size, uint64_t* module);
+/* Replaces unloadModule (CudaNativeBindings.java:60-62; native/src/jni_cuda_driver.cpp:504). */
+int f4s_unload_module(uint64_t context, uint64_t module);
+/* Replaces resolveFunction (CudaNativeBindings.java:64-67; native/src/jni_cuda_driver.cpp:524). */
+int f4s_resolve_function(uint64_t context, uint64_t module, const char* name, uint64_t* function);
+/* Replaces queryFunctionAttributes (CudaNativeBindings.java:69-71; native/src/jni_cuda_driver.cpp:548);
+ * attributes = {max threads per block, static smem, const bytes, local
+ * bytes, registers per thread}. */
+int f4s_query_function_attributes(uint64_t context, uint64_t function, int32_t attributes[5]);
+
+/* ------------------------------------------------------ streams, events */
+
+/* Replace createStream / destroyStream / synchronizeStream
+ * (CudaNativeBindings.java:73-83; native/src/jni_cuda_driver.cpp:568-627); flags 0
+ * (default) or 1 (non-blocking). */
+int f4s_create_stream(uint64_t context, int32_t flags, uint64_t* stream);
+int f4s_destroy_stream(uint64_t context, uint64_t stream);
+int f4s_synchronize_stream(uint64_t context, uint64_t stream);
+
+/* Replace createEvent / destroyEvent / recordEvent / queryEvent /
+ * synchronizeEvent / waitForEvent (CudaNativeBindings.java:85-109;
+ * native/src/jni_cuda_driver.cpp:628-749); flags
+ * may combine 1 (blocking sync) and 2 (disable timing). */
+int f4s_create_event(uint64_t context, int32_t flags, uint64_t* event);
+int f4s_destroy_event(uint64_t context, uint64_t event);
+int f4s_record_event(uint64_t context, uint64_t event, uint64_t stream);
+int f4s_query_event(uint64_t context, uint64_t event, int32_t* complete);
+int f4s_synchronize_event(uint64_t context, uint64_t event);
+int f4s_wait_for_event(uint64_t context, uint64_t stream, uint64_t event);
+/* Addition: elapsed milliseconds between two recorded timing events (the
+ * reference's event modes all disable timing, CudaResources.scala:104-106). */
+int f4s_event_elapsed_ms(uint64_t context, uint64_t start_event, uint64_t end_event, float* milliseconds);
+
+/* --------------------------------------------------------------- memory */
+
+/* Replace allocatePinnedMemory / freePinnedMemory / allocateDeviceMemory /
+ * freeDeviceMemory (CudaNativeBindings.java:111-125; native/src/jni_cuda_driver.cpp:750-829). */
+int f4s_allocate_pinned_memory(uint64_t context, uint64_t size_bytes, void** host_address);
+int f4s_free_pinned_memory(uint64_t context, void* host_address);
+int f4s_allocate_device_memory(uint64_t context, uint64_t size_bytes, uint64_t* device_address);
+int f4s_free_device_memory(uint64_t context, uint64_t device_address);
+
+/* Replace copyHostToDevice(/Async) and copyDeviceToHost(/Async)
+ * (CudaNativeBindings.java:127-151; native/src/jni_cuda_driver.cpp:830-935); the JNI direct buffer becomes
+ * (host pointer, size_bytes).  The synchronous forms block. */
+int f4s_copy_host_to_device(uint64_t context, uint64_t device_address, uint64_t device_offset_bytes,
+                            const void* source, uint64_t size_bytes);
+int f4s_copy_host_to_device_async(uint64_t context, uint64_t device_address, uint64_t device_offset_bytes,
+                                  const void* source, uint64_t size_bytes, uint64_t stream);
+int f4s_copy_device_to_host(uint64_t context, uint64_t device_address, uint64_t device_offset_bytes,
+                            void* destination, uint64_t size_bytes);
+int f4s_copy_device_to_host_async(uint64_t context, uint64_t device_address, uint64_t device_offset_bytes,
+                                  void* destination, uint64_t size_bytes, uint64_t stream);
+
+/* ------------------------------------------------------ hot-path module */
+
+typedef struct f4s_hotpath f4s_hotpath;
+
+/* Loads the embedded sm_100a module into `context` and sizes launch shapes
+ * for its device.  The module is what `CudaContext.load` would return for
+ * these kernels (runtime/src/main/scala/flight4s/runtime/cuda/CudaResources.scala:137-167). */
+int f4s_hotpath_open(uint64_t context, f4s_hotpath** hotpath);
+int f4s_hotpath_close(f4s_hotpath* hotpath);
+/* Module handle, for f4s_resolve_function / f4s_launch_kernel. */
+uint64_t f4s_hotpath_module(const f4s_hotpath* hotpath);
+int f4s_hotpath_sm_count(const f4s_hotpath* hotpath);
+/* CTAs per cluster of the full-array reductions (1..8, default 4). */
+int f4s_hotpath_set_reduce_cluster(f4s_hotpath* hotpath, int32_t cluster);
+
+/* ---------------------------------------------- full-array reductions */
+
+/* Workspace (device bytes) every reduction on this hotpath needs: a ticket
+ * counter plus one 16-byte partial per cluster.  Allocate it once, zeroed;
+ * each launch leaves it zeroed again.  Launches sharing one workspace must
+ * be ordered (same stream or events). */
+uint64_t f4s_reduce_workspace_bytes(const f4s_hotpath* hotpath);
+
+/* Parallel lowering of the reference's `ReduceSum`
+ * (core/src/main/scala/flight4s/core/ir/IR.scala:96-107) over in[0, n):
+ *   sum_f32:    *out (f64) = sum in[i], f32 values accumulated in f64;
+ *   sum_i32:    *out (i32) = sum in[i], two's-complement wrap (bit-exact);
+ *   argmax_f32: out[0] (i64) = (signed totalOrder key of the max << 32) | (0xFFFFFFFF - index),
+ *               so the int64 max of packed keys from several devices is again
+ *               (max value, lowest index); INT64_MIN if n == 0;
+ *               out[1] (i64) = index of the first maximum (+ index_base), -1 if n == 0.
+ *               The totalOrder key is bits ^ ((bits >> 31) & 0x7FFFFFFF) read as i32.
+ * With accumulate != 0 the result is combined with the value already in
+ * `out` (chunked or sharded inputs).  One launch; asynchronous on `stream`. */
+int f4s_reduce_sum_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, uint64_t n, uint64_t out,
+                       uint64_t workspace, uint64_t workspace_bytes, int32_t accumulate);
+int f4s_reduce_sum_i32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, uint64_t n, uint64_t out,
+                       uint64_t workspace, uint64_t workspace_bytes, int32_t accumulate);
+int f4s_reduce_argmax_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, uint64_t n, uint64_t out,
+                          uint64_t workspace, uint64_t workspace_bytes, uint64_t index_base,
+                          int32_t accumulate);
+
+/* End-to-end form over a HOST buffer (pinned for overlap): chunked
+ * host->device copies on `copy_stream` overlapped with the reduction on
+ * `compute_stream` through `staging` (device, >= 768 bytes, 256-aligned),
+ * result written to `host_out` (8 / 4 / 16 bytes as above).  op: 0 sum_f32,
+ * 1 sum_i32, 2 argmax_f32.  Synchronizes both streams before returning. */
+int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint64_t n, void* host_out,
+                    uint64_t staging, uint64_t staging_bytes, uint64_t workspace, uint64_t workspace_bytes,
+                    uint64_t copy_stream, uint64_t compute_stream);
+
+/* ------------------------------------------------------------ block sum */
+
+/* The reference's blockReduceSum
+ * (runtime/src/test/scala/flight4s/runtime/cuda/CudaResourcesJniSuite.scala:229-312)
+ * extended to n elements: partials[t] = fp32 tree sum of tile t (256
+ * elements, zero padded, the reference's stride order 128..1), then the same
+ * tree over runs of 256 partials until one value remains in out[0].
+ * Bit-identical to the reference kernel applied level by level. */
+uint64_t f4s_block_reduce_workspace_bytes(int32_t n);
+int f4s_block_reduce_sum_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, int32_t n, uint64_t partials,
+                             uint64_t out, uint64_t workspace, uint64_t workspace_bytes);
+
+/* ---------------------------------------------------------- elementwise */
+
+/* The reference's vectorAdd (CudaResourcesJniSuite.scala:108-227; generated
+ * text core/src/test/scala/flight4s/core/codegen/CudaCodegenSuite.scala:15-61):
+ * output[i] = left[i] + right[i] for i < element_count.  The bf16 form
+ * rounds the f32 sum to nearest-even. */
+int f4s_vector_add_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t left, uint64_t right, uint64_t output,
+                       int32_t element_count);
+int f4s_vector_add_bf16(f4s_hotpath* hotpath, uint64_t stream, uint64_t left, uint64_t right, uint64_t output,
+                        int32_t element_count);
+
+/* ------------------------------------------------------------ row-wise */
+
+/* bf16 [rows x cols] row-major, f32 math, bf16 round-to-nearest-even out:
+ *   softmax: y = exp(x - max_row) / sum_row exp(x - max_row)
+ *   rmsnorm: y = (x * rsqrt(mean_row(x^2) + eps)) * weight[col]        */
+int f4s_softmax_rows_bf16(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, uint64_t out, int32_t rows,
+                          int32_t cols);
+int f4s_rmsnorm_rows_bf16(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, uint64_t weight, uint64_t out,
+                          int32_t rows, int32_t cols, float eps);
+
+/* ------------------------------------------------------------------ fp8 */
+
+/* 1x128 block quantization of bf16 [rows x cols] to E4M3 with fused amax
+ * (element conversion = the reference's convert.f32ToFP8E4M3, saturating,
+ * round-to-nearest-even; core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:525-538):
+ *   scales[r][b] = amax_b / 448, codes = e4m3(x * min(448 / amax_b, FLT_MAX))
+ *   (0 when amax_b == 0); dequantize: y = bf16(f32(code) * scale).
+ * codes: u8 [rows x cols]; scales: f32 [rows x ceil(cols / 128)]. */
+int f4s_fp8_quantize_e4m3(f4s_hotpath* hotpath, uint64_t stream, uint64_t x, uint64_t codes, uint64_t scales,
+                          int32_t rows, int32_t cols);
+int f4s_fp8_dequantize_e4m3(f4s_hotpath* hotpath, uint64_t stream, uint64_t codes, uint64_t scales,
+                            uint64_t y, int32_t rows, int32_t cols);
+
+/* ---------------------------------------------------- synthetic inputs */
+
+/* Philox4x32-10 synthetic data, elements [offset, offset + n) of the global
+ * stream (so shards of one logical array can be generated per device).
+ * kind: 0 uniform f32 [-1,1), 1 same as bf16, 2 normal f32 (p0 mean, p1 sd),
+ * 3 normal bf16, 4 uniform i32 [ilo, ihi], 5 normal bf16 with outliers
+ * (probability p2, factor p3). */
+int f4s_fill_synthetic(f4s_hotpath* hotpath, uint64_t stream, uint64_t out, uint64_t n, uint64_t offset,
+                       uint64_t seed, uint32_t stream_id, int32_t kind, float p0, float p1, float p2, float p3,
+                       int32_t ilo, int32_t ihi);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* FLIGHT4S_B200_H_ */

@@ -1,0 +1,419 @@
+/*
+ * CPU oracle for the flight4s hot path — TEST INFRASTRUCTURE ONLY.
+ *
+ * Plain-C restatement of the reference's CPU-side checks and of the
+ * arithmetic the hot-path kernels define.  Only the test suite, the smoke
+ * check and the benchmark's CPU-baseline leg load this library; the
+ * product path never does.
+ *
+ * Pinning (what each part is checked against):
+ *   - vectorAdd and the sequential fp32 fold restate the reference's own CPU
+ *     checks: Array.tabulate(n)(i => l(i) + r(i)) and `inputValues.sum`
+ *     (runtime/src/test/scala/flight4s/runtime/cuda/CudaResourcesJniSuite.scala:114-122,235-238),
+ *     pinned by that suite's known answers (c[i] = 3i for n = 1024; 896.0
+ *     for x[i] = i % 8, n = 256);
+ *   - the block tree restates the generated blockReduceSum text
+ *     (core/src/test/scala/flight4s/core/codegen/CudaCodegenSuite.scala:133-216);
+ *   - E4M3 and bf16 conversions are written from the OCP FP8 and IEEE-754
+ *     definitions and pinned against the conversion functions the
+ *     reference's generated code calls (__nv_cvt_float_to_fp8 with
+ *     __NV_SATFINITE/__NV_E4M3 and __float2bfloat16_rn,
+ *     core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:518-538),
+ *     run on the host by tests/golden/make_golden_conversions.cpp;
+ *   - max/argmax, softmax, RMSNorm and the FP8 block scaling have no
+ *     reference implementation: parity unpinned for those, the oracle is
+ *     their definition.
+ *
+ * Compile with -ffp-contract=off: every float operation here is one IEEE
+ * single or double rounding, in source order.
+ */
+#include "oracle.h"
+
+#include <float.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------- bit casts */
+static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* --------------------------------------------------------------- Philox
+ * Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11): 10 rounds of
+ * (hi0,lo0) = M0*c0, (hi1,lo1) = M1*c2,
+ * c = (hi1^c1^k0, lo1, hi0^c3^k1, lo0), key += (W0, W1). */
+void orc_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], uint32_t out[4]) {
+  uint32_t c0 = ctr_in[0], c1 = ctr_in[1], c2 = ctr_in[2], c3 = ctr_in[3];
+  uint32_t k0 = key_in[0], k1 = key_in[1];
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0;
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+    c0 = n0;
+    c1 = (uint32_t)p1;
+    c2 = n2;
+    c3 = (uint32_t)p0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+static uint32_t philox_word(uint64_t index, uint32_t stream, uint64_t seed) {
+  const uint64_t g = index / 4;
+  const uint32_t ctr[4] = {(uint32_t)g, (uint32_t)(g >> 32), stream, 0u};
+  const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  uint32_t w[4];
+  orc_philox4x32_10(ctr, key, w);
+  return w[index % 4];
+}
+
+void orc_fill_uniform_f32(float* out, uint64_t n, uint64_t offset, uint64_t seed, uint32_t stream) {
+  for (uint64_t i = 0; i < n; ++i) {
+    const uint32_t w = philox_word(offset + i, stream, seed);
+    out[i] = (float)(w >> 8) * 0x1p-23f - 1.0f;
+  }
+}
+
+void orc_fill_uniform_i32(int32_t* out, uint64_t n, uint64_t offset, uint64_t seed, uint32_t stream,
+                          int32_t lo, int32_t hi) {
+  const uint32_t span = (uint32_t)(hi - lo) + 1u;
+  for (uint64_t i = 0; i < n; ++i) out[i] = lo + (int32_t)(philox_word(offset + i, stream, seed) % span);
+}
+
+/* ----------------------------------------------------------------- bf16
+ * IEEE-754 round-to-nearest-even of the top 16 bits; NaN -> 0x7FFF. */
+uint16_t orc_f32_to_bf16_rn(float f) {
+  const uint32_t u = f2u(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFF;
+  const uint32_t bias = 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)((u + bias) >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
+
+/* ----------------------------------------------------------------- E4M3
+ * OCP 8-bit floating point, E4M3: bias 7, 3 mantissa bits, no infinities,
+ * NaN = S.1111.111, max finite 448 = 1.75 * 2^8, min normal 2^-6,
+ * subnormals m * 2^-9.  Round to nearest even; with saturation, every
+ * finite or infinite magnitude above 448 becomes 448; NaN -> 0x7F. */
+uint8_t orc_f32_to_e4m3_satfinite(float f) {
+  if (isnan(f)) return 0x7F;
+  const uint8_t sign = (f2u(f) >> 31) ? 0x80 : 0x00;
+  const double a = fabs((double)f);
+  if (a > 448.0) return sign | 0x7E;
+  if (a < 0x1p-6) {
+    /* subnormal grid m * 2^-9, m in [0, 8]; m == 8 is the min normal 0x08 */
+    const double m = nearbyint(a * 512.0);
+    return sign | (uint8_t)m;
+  }
+  int k;
+  const double frac = frexp(a, &k); /* a = frac * 2^k, frac in [0.5, 1) */
+  int e = k - 1;                    /* a = (2 * frac) * 2^e */
+  double q = nearbyint(frac * 16.0); /* (2*frac) * 8, in [8, 16] */
+  if (q == 16.0) {
+    q = 8.0;
+    e += 1;
+  }
+  /* a <= 448 guarantees e <= 8 and (e == 8 => q <= 14) */
+  return sign | (uint8_t)(((e + 7) << 3) | ((int)q - 8));
+}
+
+float orc_e4m3_to_f32(uint8_t c) {
+  const int s = c >> 7, e = (c >> 3) & 0xF, m = c & 7;
+  if (e == 0xF && m == 7) return s ? -NAN : NAN;
+  const double v = e == 0 ? ldexp((double)m, -9) : ldexp(1.0 + m / 8.0, e - 7);
+  return (float)(s ? -v : v);
+}
+
+/* ----------------------------------------------------------- vectorAdd
+ * Array.tabulate(n)(i => l(i) + r(i)) (CudaResourcesJniSuite.scala:120-122). */
+void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) c[i] = a[i] + b[i];
+}
+
+/* bf16: widen exactly, add in f32 (one rounding), round to nearest-even. */
+void orc_vector_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) c[i] = orc_f32_to_bf16_rn(orc_bf16_to_f32(a[i]) + orc_bf16_to_f32(b[i]));
+}
+
+/* ---------------------------------------------------------- reductions
+ * Scala's Array[Float].sum: a left fold in Float from 0.0f
+ * (CudaResourcesJniSuite.scala:238). */
+float orc_sum_f32_sequential(const float* x, int64_t n) {
+  float acc = 0.0f;
+  for (int64_t i = 0; i < n; ++i) acc += x[i];
+  return acc;
+}
+
+/* Ground truth: compensated (Neumaier) summation in long double. */
+double orc_sum_f32_exactish(const float* x, int64_t n, double* abs_sum) {
+  long double s = 0.0L, c = 0.0L, a = 0.0L;
+  for (int64_t i = 0; i < n; ++i) {
+    const long double v = x[i];
+    const long double t = s + v;
+    if (fabsl(s) >= fabsl(v)) c += (s - t) + v; else c += (v - t) + s;
+    s = t;
+    a += fabsl(v);
+  }
+  if (abs_sum) *abs_sum = (double)a;
+  return (double)(s + c);
+}
+
+/* I32 accumulates in I32 with two's-complement wrap
+ * (core/src/main/scala/flight4s/core/types/CudaType.scala:204-206). */
+int32_t orc_sum_i32(const int32_t* x, int64_t n) {
+  uint32_t acc = 0;
+  for (int64_t i = 0; i < n; ++i) acc += (uint32_t)x[i];
+  return (int32_t)acc;
+}
+
+/* Signed-int image of IEEE-754 totalOrder. */
+static int32_t total_order_key(float v) {
+  const int32_t b = (int32_t)f2u(v);
+  return b ^ (int32_t)((uint32_t)(b >> 31) >> 1);
+}
+
+/* max under totalOrder, first (lowest) index on ties; -1 when n == 0. */
+int64_t orc_argmax_f32(const float* x, int64_t n, float* max_value) {
+  int64_t best = -1;
+  int32_t key = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const int32_t k = total_order_key(x[i]);
+    if (best < 0 || k > key) {
+      key = k;
+      best = i;
+    }
+  }
+  if (max_value) *max_value = best >= 0 ? x[best] : NAN;
+  return best;
+}
+
+/* Packed cross-device key, compared as a signed 64-bit integer:
+ * (signed totalOrder key << 32) | (0xFFFFFFFF - index). */
+int64_t orc_argmax_packed_key(float value, int64_t index) {
+  const uint64_t hi = (uint64_t)(uint32_t)total_order_key(value) << 32;
+  return (int64_t)(hi | (uint64_t)(0xFFFFFFFFu - (uint32_t)index));
+}
+
+/* --------------------------------------------------------- block tree
+ * One node = the reference's shared-memory tree over 256 values
+ * (strides 128, 64, ..., 1: s[t] += s[t + stride] for t < stride). */
+static float tree256(float s[256]) {
+  for (int stride = 128; stride >= 1; stride >>= 1)
+    for (int t = 0; t < stride; ++t) s[t] = s[t] + s[t + stride];
+  return s[0];
+}
+
+/* partials[t] = node over tile t (zero padded); then nodes over runs of 256
+ * partials, level by level, until one value remains (a single tile is the
+ * result itself).  n == 0 gives +0.0. */
+float orc_block_tree_sum_f32(const float* x, int64_t n, float* partials) {
+  const int64_t tiles = (n + 255) / 256;
+  if (tiles == 0) return 0.0f;
+  float* level = (float*)malloc(sizeof(float) * (size_t)tiles);
+  float s[256];
+  for (int64_t t = 0; t < tiles; ++t) {
+    for (int k = 0; k < 256; ++k) {
+      const int64_t i = t * 256 + k;
+      s[k] = i < n ? x[i] : 0.0f;
+    }
+    level[t] = tree256(s);
+    if (partials) partials[t] = level[t];
+  }
+  int64_t count = tiles;
+  while (count > 1) {
+    const int64_t nodes = (count + 255) / 256;
+    for (int64_t g = 0; g < nodes; ++g) {
+      for (int k = 0; k < 256; ++k) {
+        const int64_t i = g * 256 + k;
+        s[k] = i < count ? level[i] : 0.0f;
+      }
+      level[g] = tree256(s);
+    }
+    count = nodes;
+  }
+  const float r = level[0];
+  free(level);
+  return r;
+}
+
+/* ------------------------------------------------------------ row ops
+ * fp64 definitions of the row ops (no reference implementation exists). */
+void orc_softmax_rows_f64(const uint16_t* x, double* y, int64_t rows, int64_t cols) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * cols;
+    double m = -INFINITY;
+    for (int64_t c = 0; c < cols; ++c) m = fmax(m, orc_bf16_to_f32(xr[c]));
+    double s = 0.0;
+    for (int64_t c = 0; c < cols; ++c) s += exp((double)orc_bf16_to_f32(xr[c]) - m);
+    for (int64_t c = 0; c < cols; ++c) y[r * cols + c] = exp((double)orc_bf16_to_f32(xr[c]) - m) / s;
+  }
+}
+
+void orc_rmsnorm_rows_f64(const uint16_t* x, const uint16_t* w, double* y, int64_t rows, int64_t cols,
+                          double eps) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * cols;
+    double ss = 0.0;
+    for (int64_t c = 0; c < cols; ++c) {
+      const double v = orc_bf16_to_f32(xr[c]);
+      ss += v * v;
+    }
+    const double inv = 1.0 / sqrt(ss / (double)cols + eps);
+    for (int64_t c = 0; c < cols; ++c)
+      y[r * cols + c] = (double)orc_bf16_to_f32(xr[c]) * inv * (double)orc_bf16_to_f32(w[c]);
+  }
+}
+
+/* ------------------------------------------------------ FP8 block quant
+ * amax = max |x| over the 128-element block (NaN ignored),
+ * scale = amax / 448 (f32), inv = amax > 0 ? min(448 / amax, FLT_MAX) : 0,
+ * code = e4m3_satfinite(x * inv) (one f32 rounding). */
+void orc_fp8_quantize(const uint16_t* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols) {
+  const int64_t bpr = (cols + 127) / 128;
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < bpr; ++b) {
+      const int64_t c0 = b * 128, c1 = c0 + 128 < cols ? c0 + 128 : cols;
+      float amax = 0.0f;
+      for (int64_t c = c0; c < c1; ++c) amax = fmaxf(amax, fabsf(orc_bf16_to_f32(x[r * cols + c])));
+      const float scale = amax / 448.0f;
+      float inv = 0.0f;
+      if (amax > 0.0f) {
+        inv = 448.0f / amax;
+        if (inv > FLT_MAX) inv = FLT_MAX;
+      }
+      scales[r * bpr + b] = scale;
+      for (int64_t c = c0; c < c1; ++c) {
+        const float v = orc_bf16_to_f32(x[r * cols + c]) * inv;
+        codes[r * cols + c] = orc_f32_to_e4m3_satfinite(v);
+      }
+    }
+  }
+}
+
+void orc_fp8_dequantize(const uint8_t* codes, const float* scales, uint16_t* y, int64_t rows, int64_t cols) {
+  const int64_t bpr = (cols + 127) / 128;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < cols; ++c) {
+      const float v = orc_e4m3_to_f32(codes[r * cols + c]) * scales[r * bpr + c / 128];
+      y[r * cols + c] = orc_f32_to_bf16_rn(v);
+    }
+}
+
+/* ------------------------------------------- multi-threaded baselines
+ * The same loops split over `threads` POSIX threads (contiguous chunks),
+ * used to time the CPU baseline on all host cores. */
+typedef struct {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t begin, end;
+  int kind;
+  double out_f;
+  int64_t out_i;
+  int32_t out_key;
+} Job;
+
+static void* run_job(void* p) {
+  Job* j = (Job*)p;
+  switch (j->kind) {
+    case 0: { /* sequential f32 fold of a chunk */
+      const float* x = (const float*)j->a;
+      float acc = 0.0f;
+      for (int64_t i = j->begin; i < j->end; ++i) acc += x[i];
+      j->out_f = acc;
+      break;
+    }
+    case 1: { /* i32 wrap sum */
+      const int32_t* x = (const int32_t*)j->a;
+      uint32_t acc = 0;
+      for (int64_t i = j->begin; i < j->end; ++i) acc += (uint32_t)x[i];
+      j->out_i = (int32_t)acc;
+      break;
+    }
+    case 2: { /* argmax */
+      const float* x = (const float*)j->a;
+      int64_t best = -1;
+      int32_t key = 0;
+      for (int64_t i = j->begin; i < j->end; ++i) {
+        const int32_t k = total_order_key(x[i]);
+        if (best < 0 || k > key) { key = k; best = i; }
+      }
+      j->out_i = best;
+      j->out_key = key;
+      break;
+    }
+    case 3: { /* vectorAdd f32 */
+      orc_vector_add_f32((const float*)j->a + j->begin, (const float*)j->b + j->begin, (float*)j->c + j->begin,
+                         j->end - j->begin);
+      break;
+    }
+    default:
+      break;
+  }
+  return NULL;
+}
+
+static void run_parallel(Job* jobs, int threads) {
+  pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+  for (int t = 1; t < threads; ++t) pthread_create(&tid[t], NULL, run_job, &jobs[t]);
+  run_job(&jobs[0]);
+  for (int t = 1; t < threads; ++t) pthread_join(tid[t], NULL);
+  free(tid);
+}
+
+static Job* split(const void* a, const void* b, void* c, int64_t n, int threads, int kind) {
+  Job* jobs = (Job*)calloc((size_t)threads, sizeof(Job));
+  for (int t = 0; t < threads; ++t) {
+    jobs[t].a = a; jobs[t].b = b; jobs[t].c = c; jobs[t].kind = kind;
+    jobs[t].begin = n * t / threads;
+    jobs[t].end = n * (t + 1) / threads;
+  }
+  return jobs;
+}
+
+double orc_mt_sum_f32(const float* x, int64_t n, int threads) {
+  if (threads < 1) threads = 1;
+  Job* jobs = split(x, NULL, NULL, n, threads, 0);
+  run_parallel(jobs, threads);
+  double s = 0.0;
+  for (int t = 0; t < threads; ++t) s += jobs[t].out_f;
+  free(jobs);
+  return s;
+}
+
+int32_t orc_mt_sum_i32(const int32_t* x, int64_t n, int threads) {
+  if (threads < 1) threads = 1;
+  Job* jobs = split(x, NULL, NULL, n, threads, 1);
+  run_parallel(jobs, threads);
+  uint32_t s = 0;
+  for (int t = 0; t < threads; ++t) s += (uint32_t)jobs[t].out_i;
+  free(jobs);
+  return (int32_t)s;
+}
+
+int64_t orc_mt_argmax_f32(const float* x, int64_t n, int threads) {
+  if (threads < 1) threads = 1;
+  Job* jobs = split(x, NULL, NULL, n, threads, 2);
+  run_parallel(jobs, threads);
+  int64_t best = -1;
+  int32_t key = 0;
+  for (int t = 0; t < threads; ++t) {
+    if (jobs[t].out_i >= 0 && (best < 0 || jobs[t].out_key > key)) {
+      key = jobs[t].out_key;
+      best = jobs[t].out_i;
+    }
+  }
+  free(jobs);
+  return best;
+}
+
+void orc_mt_vector_add_f32(const float* a, const float* b, float* c, int64_t n, int threads) {
+  if (threads < 1) threads = 1;
+  Job* jobs = split(a, b, c, n, threads, 3);
+  run_parallel(jobs, threads);
+  free(jobs);
+}

@@ -1,0 +1,88 @@
+"""The oracle against the reference's golden vectors and known answers."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _conversions():
+    raw = (GOLDEN / "conversions.bin").read_bytes()
+    n = int(np.frombuffer(raw[:4], np.uint32)[0])
+    inputs = np.frombuffer(raw[4:4 + 4 * n], np.uint32)
+    e4m3 = np.frombuffer(raw[4 + 4 * n:4 + 5 * n], np.uint8)
+    bf16 = np.frombuffer(raw[4 + 5 * n:4 + 7 * n], np.uint16)
+    return inputs.view(np.float32), e4m3, bf16
+
+
+def test_e4m3_encoder_matches_cuda_conversion_golden():
+    """Golden codes from __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3),
+    the call the reference's codegen emits (CudaCodegen.scala:525-538)."""
+    x, codes, _ = _conversions()
+    ours = np.array([orc.lib.orc_f32_to_e4m3_satfinite(float(v)) for v in x], np.uint8)
+    bad = np.nonzero(ours != codes)[0]
+    assert bad.size == 0, [(hex(x.view(np.uint32)[i]), hex(ours[i]), hex(codes[i])) for i in bad[:10]]
+
+
+def test_bf16_encoder_matches_cuda_conversion_golden():
+    """Golden bits from __float2bfloat16_rn (CudaCodegen.scala:518-523)."""
+    x, _, bf16 = _conversions()
+    ours = np.array([orc.lib.orc_f32_to_bf16_rn(float(v)) for v in x], np.uint16)
+    assert np.array_equal(ours, bf16)
+    assert np.array_equal(orc._vec_bf16(np.ascontiguousarray(x)), bf16)
+
+
+def test_exhaustive_conversion_check_recorded_zero_mismatches():
+    text = (GOLDEN / "conversions_exhaustive.txt").read_text()
+    assert "fp32 patterns checked: 4294967296" in text
+    assert "e4m3 satfinite rn mismatches: 0" in text
+    assert "bf16 rn mismatches (non-NaN): 0" in text
+
+
+def test_e4m3_decode_table():
+    t = orc.E4M3_TABLE
+    assert t[0x00] == 0.0 and t[0x7E] == 448.0 and t[0xFE] == -448.0
+    assert t[0x01] == 2.0 ** -9 and t[0x08] == 2.0 ** -6
+    assert np.isnan(t[0x7F]) and np.isnan(t[0xFF])
+    finite = t[np.isfinite(t)]
+    # every finite code round-trips through the encoder
+    for c in range(256):
+        if np.isfinite(t[c]) and not (c == 0x80):
+            assert orc.lib.orc_f32_to_e4m3_satfinite(float(t[c])) == c
+    assert finite.size == 254
+
+
+def test_philox_known_answer_vectors():
+    """Random123 Philox4x32-10 known-answer tests."""
+    assert orc.philox([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    assert orc.philox([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2) == [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]
+    assert orc.philox([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0]) == \
+        [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
+
+
+def test_uniform_streams_are_shardable():
+    whole = orc.uniform_f32(1000, seed=0x5EED)
+    parts = np.concatenate([orc.uniform_f32(333, 0x5EED, 0), orc.uniform_f32(667, 0x5EED, 333)])
+    assert np.array_equal(whole, parts)
+    assert whole.min() >= -1.0 and whole.max() < 1.0
+    ints = orc.uniform_i32(10000, 0x5EED, -1000, 1000)
+    assert ints.min() >= -1000 and ints.max() <= 1000
+
+
+def test_reference_known_answers():
+    """CudaResourcesJniSuite.scala: vectorAdd (:114-122) and block sum (:235-238, :310)."""
+    ka = json.loads((GOLDEN / "reference_known_answers.json").read_text())
+    n = ka["vector_add"]["n"]
+    a = np.arange(n, dtype=np.float32)
+    b = (np.arange(n) * 2).astype(np.float32)
+    c = orc.vector_add_f32(a, b)
+    assert c[:8].tolist() == ka["vector_add"]["expected_first"]
+    assert float(c.astype(np.float64).sum()) == ka["vector_add"]["expected_sum_of_outputs"]
+    x = (np.arange(ka["block_reduce_sum"]["n"]) % 8).astype(np.float32)
+    assert orc.sum_f32_sequential(x) == ka["block_reduce_sum"]["expected"]
+    total, partials = orc.block_tree_sum_f32(x)
+    assert total == ka["block_reduce_sum"]["expected"] and partials.tolist() == [896.0]
