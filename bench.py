@@ -1,0 +1,465 @@
+"""Benchmark of the flight4s hot path on B200.
+
+Headline workload (one "step"): the three full-array reductions over
+n = 2^32 elements sharded contiguously over the N GPUs of one node
+(strong scaling: the total is fixed at 2^32 per array):
+    sum f32 (N(0,1), f64 accumulation), max/argmax f32 (same array),
+    sum i32 (uniform [-1000, 1000]),
+each one kernel launch per GPU followed, for N > 1, by one NCCL all_reduce
+of the per-GPU partial.  Algorithmic bytes: 4 B per element per reduction,
+48 GiB per step in total.  Inputs (16 GiB per array) are far larger than
+L2 (126 MB), so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line.  `value` is device-resident whole-job GB/s
+(inputs already in HBM); `e2e` is the same step through the public
+host-buffer call (f4s_reduce_host: pinned host -> device copies inside the
+timed region).  At N = 1 the line also carries a per-kernel table for the
+other hot-path kernels (vectorAdd, block sum, softmax, RMSNorm, FP8).
+`--impl reference` times the CPU restatement of the reference's path (the
+oracle port, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime as _dt
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_TOTAL = 1 << 32
+SEED = 0x5EED
+HBM_PEAK_FALLBACK = 6650.0
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return HBM_PEAK_FALLBACK, "fallback"
+
+
+def _traffic_table() -> dict:
+    """Per-launch DRAM bytes per element from the committed ncu summary."""
+    p = ROOT / "profiles" / "dram_traffic.txt"
+    out = {}
+    if p.exists():
+        for line in p.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, gpus: str):
+        self.path = Path(f"/tmp/f4s_clocks_{os.getpid()}.csv")
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpus}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.windows: list[tuple[float, float]] = []
+
+    def mark(self, t0: float, t1: float):
+        self.windows.append((t0, t1))
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                ts = _dt.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[2]), float(f[3]), f[6:10]))
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        inside = [r for r in rows if any(a - 0.05 <= r[0] <= b + 0.05 for a, b in self.windows)]
+        use = inside or rows
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        mhz = sorted(r[1] for r in use)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in use for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[2] for r in use), "reasons": reasons,
+                "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+# ------------------------------------------------------------ CPU legs
+def cpu_reference_run(n: int, steps: int, warmup: int, threads: int) -> dict:
+    """The reference's CPU path restated (oracle): per-thread sequential
+    Float folds (Array.sum), argmax and Int sum over `n` elements each."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    rng = np.random.default_rng(SEED)
+    x = rng.standard_normal(n, dtype=np.float32)
+    xi = rng.integers(-1000, 1001, n, dtype=np.int32)
+    times = []
+    for k in range(warmup + steps):
+        t0 = time.perf_counter()
+        orc.lib.orc_mt_sum_f32(x.ctypes.data, n, threads)
+        orc.lib.orc_mt_argmax_f32(x.ctypes.data, n, threads)
+        orc.lib.orc_mt_sum_i32(xi.ctypes.data, n, threads)
+        t1 = time.perf_counter()
+        if k >= warmup:
+            times.append(t1 - t0)
+    sec = sum(times) / len(times)
+    gbs = 3 * 4 * n / sec / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"sum f32 + argmax f32 + sum i32 over 2^{n.bit_length() - 1} elements each, "
+                      f"{steps} timed passes", "ms_per_step": sec * 1e3,
+            "elements_per_s": 3 * n / sec}
+
+
+# ------------------------------------------------------- GPU headline
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel table")
+    ap.add_argument("--cpu-sample-log2", type=int, default=28)
+    ap.add_argument("--e2e-max-log2", type=int, default=30,
+                    help="cap on the per-rank host sample of each array in the e2e leg (pinned host memory)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    threads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = cpu_reference_run(1 << args.cpu_sample_log2, args.steps, args.warmup, threads)
+        line = {"metric": "achieved HBM GB/s", "value": r["value"], "unit": "GB/s", "impl": "reference",
+                "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32/i32", "data": "synthetic (seeded numpy)",
+                "elements_per_s": r["elements_per_s"],
+                "config": {"workload": "full-array sum f32 + max/argmax f32 + sum i32 (reference CPU path, "
+                                       "bounded sample)", "n": 1 << args.cpu_sample_log2},
+                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import flight4s_b200 as f4s
+    from flight4s_b200.sharded import ShardedReducer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300))
+    ctx = f4s.CudaContext.open(local)
+    hp = ctx.hotpath()
+    red = ShardedReducer(hp, dev, N_TOTAL)
+    count, offset = red.count, red.offset
+    stream = torch.cuda.current_stream()
+
+    x = torch.empty(count, dtype=torch.float32, device=dev)
+    xi = torch.empty(count, dtype=torch.int32, device=dev)
+    hp.fill_synthetic(x, count, f4s.NORMAL_F32, seed=SEED, offset=offset, stream=stream)
+    hp.fill_synthetic(xi, count, f4s.UNIFORM_I32, seed=SEED, offset=offset, ilo=-1000, ihi=1000, stream=stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    ops = [("f4s_reduce_sum_f32", lambda: red.sum_f32_async(x, stream)),
+           ("f4s_reduce_argmax_f32", lambda: red.argmax_f32_async(x, stream)),
+           ("f4s_reduce_sum_i32", lambda: red.sum_i32_async(xi, stream))]
+
+    for _ in range(args.warmup):
+        for _, op in ops:
+            op()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(visible if visible else ",".join(str(i) for i in range(world))) if rank == 0 else None
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    time.sleep(0.3)  # let the sampler start
+    # per-kernel events inside the timed region (the kernel-only roofline)
+    kev = {name: [] for name, _ in ops}
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_host0 = time.time()
+    start.record(stream)
+    for _ in range(args.steps):
+        for name, op in ops:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            op()
+            b.record(stream)
+            kev[name].append((a, b))
+    end.record(stream)
+    torch.cuda.synchronize()
+    t_host1 = time.time()
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark(t_host0, t_host1)
+    ms_local = start.elapsed_time(end)
+    ms_t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_total = float(ms_t.item())
+    ms_step = ms_total / args.steps
+    # per-kernel average (each interval spans the kernel plus, for N > 1, its all_reduce;
+    # the kernel alone is timed at N = 1 and in the table below)
+    kernel_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / len(evs) for name, evs in kev.items()}
+
+    # results of the last step (checked against torch on the full array at N = 1)
+    s_val = float(red.f64.item())
+    i_val = int(red.i32.item())
+    v_max, i_max = ShardedReducer.argmax_result(red.arg)
+    verified = None
+    if world == 1:
+        ref_i = int(torch.sum(xi, dtype=torch.int64).item())
+        ok_i = i_val == (ref_i + 2**31) % 2**32 - 2**31
+        ok_a = i_max == int(torch.argmax(x).item())
+        ref_s = torch.sum(x, dtype=torch.float64).item()
+        abs_s = torch.sum(x.abs(), dtype=torch.float64).item()
+        ok_s = abs(s_val - ref_s) <= 1e-5 * abs_s
+        verified = bool(ok_i and ok_a and ok_s)
+
+    peak, peak_kind = _peaks()
+    bytes_step = 3 * 4 * N_TOTAL
+    value = bytes_step / (ms_step / 1e3) / 1e9
+    elements_s = 3 * N_TOTAL / (ms_step / 1e3)
+
+    # ---- e2e through the host-buffer public call
+    e2e = None
+    try:
+        e2e = run_e2e(ctx, hp, red, x, xi, min(count, 1 << args.e2e_max_log2), world, dev, args.e2e_steps, barrier)
+    except Exception as exc:  # reported, not hidden
+        e2e = {"value": None, "unit": "GB/s", "error": f"{type(exc).__name__}: {exc}"}
+    del x, xi
+    torch.cuda.empty_cache()
+
+    kernels = None
+    if world == 1 and not args.no_kernels:
+        kernels = kernel_table(ctx, hp, dev, peak)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    clocks = sampler.summary() if sampler else None
+    dominant = max(kernel_ms, key=kernel_ms.get)
+    per_launch_bytes = 4 * count
+    achieved = per_launch_bytes / (kernel_ms[dominant] / 1e3) / 1e9
+    traffic_per_elem = _traffic_table().get(dominant)
+    cpu = cpu_reference_run(1 << args.cpu_sample_log2, 3, 1, threads) if world == 1 else None
+    line = {
+        "metric": "achieved HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32/i32", "data": "synthetic (device Philox: N(0,1) f32, U[-1000,1000] i32)",
+        "elements_per_s": elements_s, "hbm_fraction": value / (peak * world),
+        "config": {"workload": "full-array sum f32 + max/argmax f32 + sum i32, n=2^32 each, sharded over GPUs",
+                   "n_total": N_TOTAL, "n_per_gpu": count, "parallelism": f"shard{world} + nccl all_reduce",
+                   "l2": "inputs 16 GiB per array >> 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm_gbs (copy) of MEASURED_PEAKS.json" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s", "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": (traffic_per_elem * count) if traffic_per_elem else None,
+                     "algorithmic_bytes_per_launch": per_launch_bytes,
+                     "kernel_ms": kernel_ms if world == 1 else None,
+                     "interval_ms_incl_allreduce": kernel_ms if world > 1 else None},
+        "results": {"sum_f32": s_val, "sum_i32": i_val, "max_f32": v_max, "argmax": i_max, "verified_vs_torch": verified},
+        "gpu_launches": 3 * args.steps * world,
+        "clocks": clocks,
+        "e2e": e2e,
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")} if cpu else None,
+        "kernels": kernels,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
+    """Same step through f4s_reduce_host: the rank's shard in pinned host
+    memory, chunked H2D copies overlapped with the kernels, the result
+    copied back to the host; for N > 1 the partials are combined across
+    ranks exactly as in the device path."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import flight4s_b200 as f4s
+    from flight4s_b200._native import check, lib
+
+    hx = ctx.allocate_pinned("f32", count)
+    hxi = ctx.allocate_pinned("i32", count)
+    check(lib.f4s_copy_device_to_host(ctx.handle, x.data_ptr(), 0, hx.address, 4 * count), "shard to host")
+    check(lib.f4s_copy_device_to_host(ctx.handle, xi.data_ptr(), 0, hxi.address, 4 * count), "shard to host")
+    staging = ctx.allocate("u8", 256 + 2 * (256 << 20))
+    s_copy, s_comp = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    base = red.offset
+
+    def step():
+        rs = hp.reduce_host(f4s.REDUCE_SUM_F32, hx.array, staging, s_copy, s_comp)
+        ra = hp.reduce_host(f4s.REDUCE_ARGMAX_F32, hx.array, staging, s_copy, s_comp, index_base=base)
+        ri = hp.reduce_host(f4s.REDUCE_SUM_I32, hxi.array, staging, s_copy, s_comp)
+        if world > 1:
+            t = torch.tensor([rs[:1].view(np.float64)[0]], dtype=torch.float64, device=dev)
+            k = torch.tensor([int(ra.view(np.int64)[0])], dtype=torch.int64, device=dev)
+            ti = torch.tensor([int(ri[:1].view(np.int32)[0])], dtype=torch.int32, device=dev)
+            dist.all_reduce(t)
+            dist.all_reduce(k, op=dist.ReduceOp.MAX)
+            dist.all_reduce(ti)
+            return t.item(), k.item(), ti.item()
+        return rs, ra, ri
+
+    step()  # warm-up
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    t1 = time.perf_counter()
+    sec = torch.tensor([(t1 - t0) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+    sec_step = float(sec.item())
+    for b in (hx, hxi):
+        b.close()
+    staging.close()
+    s_copy.close()
+    s_comp.close()
+    return {"value": 3 * 4 * count * world / sec_step / 1e9, "unit": "GB/s",
+            "h2d_bytes_per_step": 3 * 4 * count * world, "d2h_bytes_per_step": (8 + 16 + 4) * world,
+            "ms_per_step": sec_step * 1e3, "steps": steps, "elements_per_rank": count,
+            "api": "f4s_reduce_host (pinned host shard, chunked H2D overlapped with the reduction kernel)"}
+
+
+def kernel_table(ctx, hp, dev, peak) -> dict:
+    """The other hot-path kernels at their BASELINE configurations, 1 GPU,
+    CUDA events around `reps` back-to-back launches after warm-up."""
+    import torch
+
+    import flight4s_b200 as f4s
+    out = {}
+    stream = torch.cuda.current_stream()
+
+    def timeit(fn, reps=20, warm=3, flush=None):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            if flush is not None:
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            times.append((a, b))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times) / len(times)
+
+    def row(name, nbytes, elems, ms, **extra):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"ms": ms, "gbs": gbs, "frac": gbs / peak, "elements_per_s": elems / (ms / 1e3),
+                     "bytes": nbytes, **extra}
+
+    n = 1 << 28
+    a = torch.empty(n, dtype=torch.float32, device=dev)
+    b = torch.empty_like(a)
+    c = torch.empty_like(a)
+    hp.fill_synthetic(a, n, f4s.UNIFORM_F32, seed=1)
+    hp.fill_synthetic(b, n, f4s.UNIFORM_F32, seed=2)
+    row("vector_add_f32 n=2^28", 12 * n, n, timeit(lambda: hp.vector_add_f32(a, b, c, stream=stream)))
+    del a, b, c
+    a = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(a)
+    c = torch.empty_like(a)
+    hp.fill_synthetic(a, n, f4s.UNIFORM_BF16, seed=1)
+    hp.fill_synthetic(b, n, f4s.UNIFORM_BF16, seed=2)
+    row("vector_add_bf16 n=2^28", 6 * n, n, timeit(lambda: hp.vector_add_bf16(a, b, c, stream=stream)))
+    del a, b, c
+
+    # block sum, n = 2^20 (4 MiB: L2-resident when hot)
+    n = 1 << 20
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    hp.fill_synthetic(x, n, f4s.UNIFORM_F32, seed=SEED)
+    parts = torch.empty(n // 256, dtype=torch.float32, device=dev)
+    o = torch.empty(1, dtype=torch.float32, device=dev)
+    ws = torch.zeros(hp.block_reduce_workspace_bytes(n), dtype=torch.uint8, device=dev)
+
+    class _W:
+        size_bytes = ws.numel()
+
+        @staticmethod
+        def data_ptr():
+            return ws.data_ptr()
+    fn = lambda: hp.block_reduce_sum_f32_into(x, parts, o, _W, stream=stream)  # noqa: E731
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    row("block_reduce_sum_f32 n=2^20 hot-L2", 4 * n + 4 * (n // 256), n, timeit(fn, reps=50))
+    row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, timeit(fn, reps=20, flush=flush))
+    del flush
+
+    rows, cols = 32768, 8192
+    xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)
+    yb = torch.empty_like(xb)
+    w = torch.empty(cols, dtype=torch.bfloat16, device=dev)
+    hp.fill_synthetic(xb, rows * cols, f4s.NORMAL_BF16, seed=SEED)
+    hp.fill_synthetic(w, cols, f4s.NORMAL_BF16, seed=SEED + 1, p0=1.0, p1=0.1)
+    row("softmax_rows_bf16 32768x8192", 4 * rows * cols, rows * cols,
+        timeit(lambda: hp.softmax_rows_bf16(xb, yb, rows, cols, stream=stream)))
+    row("rmsnorm_rows_bf16 32768x8192", 4 * rows * cols + 2 * cols, rows * cols,
+        timeit(lambda: hp.rmsnorm_rows_bf16(xb, w, yb, rows, cols, 1e-6, stream=stream)))
+    del xb, yb, w
+
+    rows = cols = 16384
+    n = rows * cols
+    xb = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    hp.fill_synthetic(xb, n, f4s.NORMAL_BF16_OUTLIERS, seed=SEED, p0=0.0, p1=2.0, p2=1e-3, p3=50.0)
+    q = torch.empty(n, dtype=torch.uint8, device=dev)
+    s = torch.empty(n // 128, dtype=torch.float32, device=dev)
+    y = torch.empty_like(xb)
+    qb = 2 * n + n + 4 * (n // 128)
+    row("fp8_quantize_e4m3 16384x16384", qb, n, timeit(lambda: hp.fp8_quantize_e4m3(xb, q, s, rows, cols, stream=stream)))
+    row("fp8_dequantize_e4m3 16384x16384", qb, n,
+        timeit(lambda: hp.fp8_dequantize_e4m3(q, s, y, rows, cols, stream=stream)))
+    del xb, q, s, y
+    torch.cuda.empty_cache()
+    return out
+
+
+if __name__ == "__main__":
+    main()

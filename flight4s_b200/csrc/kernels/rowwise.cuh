@@ -98,13 +98,14 @@ __device__ __forceinline__ void softmax_row_regs(const uint16_t* in, uint16_t* o
 #pragma unroll
       for (int j = 0; j < 8; ++j) m = fmaxf(m, x[k * 8 + j]);
   m = block_max(m, red_a);
-  const float ms = m * kLog2e;
   float s = 0.0f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float e = valid[k] ? fast_exp2(fmaf(x[k * 8 + j], kLog2e, -ms)) : 0.0f;
+      // (x - m) first: folding m into an FMA (x*log2e - m*log2e) cancels
+      // catastrophically when |m| is large.
+      const float e = valid[k] ? fast_exp2((x[k * 8 + j] - m) * kLog2e) : 0.0f;
       x[k * 8 + j] = e;
       s += e;
     }
@@ -193,14 +194,13 @@ f4s_softmax_rows_bf16_any(const uint16_t* __restrict__ in, uint16_t* __restrict_
     for (int c = threadIdx.x; c < cols; c += kRowBlock)
       m = fmaxf(m, __uint_as_float(static_cast<uint32_t>(x[c]) << 16));
     m = block_max(m, red_a);
-    const float ms = m * kLog2e;
     float s = 0.0f;
     for (int c = threadIdx.x; c < cols; c += kRowBlock)
-      s += fast_exp2(fmaf(__uint_as_float(static_cast<uint32_t>(x[c]) << 16), kLog2e, -ms));
+      s += fast_exp2((__uint_as_float(static_cast<uint32_t>(x[c]) << 16) - m) * kLog2e);
     s = block_sum(s, red_b);
     const float inv = 1.0f / s;
     for (int c = threadIdx.x; c < cols; c += kRowBlock) {
-      const float e = fast_exp2(fmaf(__uint_as_float(static_cast<uint32_t>(x[c]) << 16), kLog2e, -ms));
+      const float e = fast_exp2((__uint_as_float(static_cast<uint32_t>(x[c]) << 16) - m) * kLog2e);
       y[c] = static_cast<uint16_t>(pack_bf16x2_rn(e * inv, 0.0f) & 0xFFFFu);
     }
     __syncthreads();

@@ -395,13 +395,14 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hp, uint64_t stream, uint64_t in, uint64_
   });
 }
 
-int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n, void* host_out,
-                    uint64_t staging, uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes, uint64_t copy_stream,
-                    uint64_t compute_stream) {
+int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
+                    void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes,
+                    uint64_t copy_stream, uint64_t compute_stream) {
   return guarded([&] {
     if (op < 0 || op > 2) throw std::invalid_argument("unknown reduction op " + std::to_string(op));
-    return op_status(hot(hp).reduce_host(static_cast<ReduceOp>(op), host_in, n, host_out, staging, staging_bytes,
-                                         ws, ws_bytes, stream_of(copy_stream), stream_of(compute_stream)));
+    return op_status(hot(hp).reduce_host(static_cast<ReduceOp>(op), host_in, n, index_base, host_out, staging,
+                                         staging_bytes, ws, ws_bytes, stream_of(copy_stream),
+                                         stream_of(compute_stream)));
   });
 }
 

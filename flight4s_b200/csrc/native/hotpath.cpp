@@ -376,7 +376,8 @@ CUresult Hotpath::fill_synthetic(CUstream stream, CUdeviceptr out, std::uint64_t
   return cur.finish(launch(function("f4s_fill_synthetic"), stream, shape_.fill_grid, 256, 0, args));
 }
 
-CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, std::uint64_t index_base,
+                              void* host_out,
                               CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
                               std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream) {
   if (n > 0 && host_in == nullptr) throw std::invalid_argument("host input must not be null");
@@ -416,7 +417,8 @@ CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n,
     if (r == CUDA_SUCCESS) r = api.cuStreamWaitEvent(compute_stream, copied[b], 0);
     if (r == CUDA_SUCCESS) {
       // Pushing the same context again inside reduce() is harmless.
-      r = reduce(op, compute_stream, buffers[b], count, result, workspace, workspace_bytes, first, k > 0 ? 1 : 0);
+      r = reduce(op, compute_stream, buffers[b], count, result, workspace, workspace_bytes, index_base + first,
+                 k > 0 ? 1 : 0);
     }
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(consumed[b], compute_stream);
   }

@@ -72,7 +72,7 @@ class Hotpath {
   // `copy_stream` overlapped with per-chunk reductions on `compute_stream`
   // (double-buffered in `staging`), result copied back to `host_out`, and
   // both streams synchronized before returning.
-  CUresult reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+  CUresult reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, std::uint64_t index_base, void* host_out,
                        CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
                        std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream);
 

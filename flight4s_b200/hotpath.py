@@ -128,13 +128,13 @@ class Hotpath:
         return unpack_argmax_key(int(r[0]))[0], index
 
     def reduce_host(self, op: int, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
-                    workspace: Any = None) -> np.ndarray:
+                    workspace: Any = None, index_base: int = 0) -> np.ndarray:
         """End-to-end reduction of a host array (pinned for overlap) through
         `staging` device memory; returns the raw 8/4/16-byte result."""
         ws = self.workspace() if workspace is None else workspace
         out = np.zeros(2, np.uint64)
         host = np.ascontiguousarray(host)
-        check(lib.f4s_reduce_host(self._h, op, host.ctypes.data, host.size, out.ctypes.data,
+        check(lib.f4s_reduce_host(self._h, op, host.ctypes.data, host.size, index_base, out.ctypes.data,
                                   device_address(staging), staging.size_bytes, device_address(ws), ws.size_bytes,
                                   stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")
         return out

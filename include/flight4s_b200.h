@@ -219,11 +219,12 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, ui
 /* End-to-end form over a HOST buffer (pinned for overlap): chunked
  * host->device copies on `copy_stream` overlapped with the reduction on
  * `compute_stream` through `staging` (device, >= 768 bytes, 256-aligned),
- * result written to `host_out` (8 / 4 / 16 bytes as above).  op: 0 sum_f32,
- * 1 sum_i32, 2 argmax_f32.  Synchronizes both streams before returning. */
-int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint64_t n, void* host_out,
-                    uint64_t staging, uint64_t staging_bytes, uint64_t workspace, uint64_t workspace_bytes,
-                    uint64_t copy_stream, uint64_t compute_stream);
+ * result written to `host_out` (8 / 4 / 16 bytes as above; argmax indices
+ * start at `index_base`).  op: 0 sum_f32, 1 sum_i32, 2 argmax_f32.
+ * Synchronizes both streams before returning. */
+int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
+                    void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t workspace,
+                    uint64_t workspace_bytes, uint64_t copy_stream, uint64_t compute_stream);
 
 /* ------------------------------------------------------------ block sum */
 

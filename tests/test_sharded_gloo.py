@@ -1,0 +1,73 @@
+"""The sharded reductions' combine step on CPU: world_size 2 gloo ranks,
+per-rank partials from the oracle, combined by the product's collectives;
+must equal the whole-array oracle results (bit-exact for i32 and argmax)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from flight4s_b200 import sharded
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, n: int, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from oracle import oracle as orc
+    x = orc.uniform_f32(n, seed=42)
+    xi = orc.uniform_i32(n, seed=42, lo=-1000, hi=1000)
+
+    def partial(rank, offset, count):
+        part = x[offset:offset + count]
+        s, _ = orc.sum_f32_exact(np.ascontiguousarray(part))
+        i = orc.sum_i32(np.ascontiguousarray(xi[offset:offset + count]))
+        v, idx = orc.argmax_f32(np.ascontiguousarray(part))
+        key = orc.argmax_packed_key(v, idx + offset) if idx >= 0 else -(1 << 63)
+        return s, i, key
+
+    out = sharded.cpu_sharded_combine(partial, n)
+    q.put((rank, out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_combine_matches_whole_array(world):
+    from oracle import oracle as orc
+    n = 100_003
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x = orc.uniform_f32(n, seed=42)
+    xi = orc.uniform_i32(n, seed=42, lo=-1000, hi=1000)
+    exact, abs_sum = orc.sum_f32_exact(x)
+    v, idx = orc.argmax_f32(x)
+    for rank in range(world):
+        s, i, key = results[rank]
+        assert abs(s - exact) <= 1e-12 * abs_sum
+        assert i == orc.sum_i32(xi)
+        assert key == orc.argmax_packed_key(v, idx)
+
+
+def test_shard_bounds_cover_exactly():
+    for n in [0, 1, 7, 2**32]:
+        for world in [1, 2, 3, 8]:
+            spans = [sharded.shard_bounds(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0
+            assert all(a[0] + a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert spans[-1][0] + spans[-1][1] == n
