@@ -2,10 +2,13 @@
 
 Steps (all in-tree so the artefacts travel with the source tree):
   1. nvcc -cubin -gencode arch=compute_100a,code=sm_100a  csrc/kernels/kernels.cu
-  2. g++ -shared  csrc/native/*.cpp + kernel_image.S (embeds the cubin)
-     -> flight4s_b200/libflight4s_b200.so
+  2. nvcc -c  csrc/native/*.cu (host code with registered device data)
+  3. g++ -shared  csrc/native/*.cpp + those objects + kernel_image.S (embeds
+     the cubin) + static CUDA runtime -> flight4s_b200/libflight4s_b200.so
 
-The library links no CUDA library: libcuda.so.1 is opened at first use.
+The library needs no CUDA shared library at load time: libcuda.so.1 is
+opened at first use, and the CUDA runtime used by the static-workspace
+entry point is linked in statically (hidden).
 """
 from __future__ import annotations
 
@@ -53,19 +56,39 @@ def build_cubin(force: bool = False, verbose: bool = False) -> Path:
     return CUBIN
 
 
+def build_runtime_objects(force: bool = False) -> list[Path]:
+    """nvcc-compiled host+device objects linked into the library (the
+    static-workspace .cu files, registered with the CUDA runtime)."""
+    native = CSRC / "native"
+    objs = []
+    nvcc = str(CUDA_HOME / "bin" / "nvcc")
+    for cu in sorted(native.glob("*.cu")):
+        obj = BUILD / (cu.stem + ".o")
+        deps = [cu] + sorted(native.glob("*.hpp"))
+        if force or not _newer(obj, deps):
+            BUILD.mkdir(exist_ok=True)
+            _run([nvcc, *NVCC_ARCH, "-O3", "-std=c++17", "-c", "-Xcompiler", "-fPIC", f"-I{native}",
+                  str(cu), "-o", str(obj)])
+        objs.append(obj)
+    return objs
+
+
 def build_library(force: bool = False, verbose: bool = False) -> Path:
     cubin = build_cubin(force=force, verbose=verbose)
+    objs = build_runtime_objects(force=force)
     native = CSRC / "native"
     sources = sorted(native.glob("*.cpp"))
-    deps = sources + sorted(native.glob("*.hpp")) + [native / "driver_functions.inc", native / "kernel_image.S",
-                                                      cubin, PKG.parent / "include" / "flight4s_b200.h"]
+    deps = sources + objs + sorted(native.glob("*.hpp")) + [native / "driver_functions.inc",
+                                                             native / "kernel_image.S", cubin,
+                                                             PKG.parent / "include" / "flight4s_b200.h"]
     if not force and _newer(LIB, deps):
         return LIB
     cxx = shutil.which("g++") or "g++"
     tmp = LIB.with_suffix(".so.tmp")
     _run([cxx, "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Wno-unused-parameter",
           f"-I{CUDA_HOME / 'include'}", f"-I{native}",
-          f'-DF4S_KERNEL_IMAGE="{cubin}"', *map(str, sources), str(native / "kernel_image.S"),
+          f'-DF4S_KERNEL_IMAGE="{cubin}"', *map(str, sources), *map(str, objs), str(native / "kernel_image.S"),
+          f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static", "-lrt", "-lpthread",
           # The C++ runtime is linked in and hidden, so the library can be
           # loaded into any host process (a JVM, Python) without its
           # libstdc++ symbols interposing with the host's.

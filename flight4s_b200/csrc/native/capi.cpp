@@ -17,6 +17,7 @@
 #include "cuda_launcher.hpp"
 #include "hotpath.hpp"
 #include "launch_contract.hpp"
+#include "noalloc_scratch.hpp"
 
 using flight4s::cuda::CudaDriver;
 using flight4s::cuda::CudaDriverStatus;
@@ -414,6 +415,13 @@ int f4s_block_reduce_sum_f32(f4s_hotpath* hp, uint64_t stream, uint64_t in, int3
                              uint64_t out, uint64_t ws, uint64_t ws_bytes) {
   return guarded(
       [&] { return op_status(hot(hp).block_sum_f32(stream_of(stream), in, n, partials, out, ws, ws_bytes)); });
+}
+
+int f4s_block_reduce_sum_f32_noalloc(f4s_hotpath* hp, uint64_t stream, uint64_t in, int32_t n, uint64_t partials,
+                                     uint64_t out) {
+  return guarded([&] {
+    return op_status(flight4s::cuda::block_sum_f32_noalloc(hot(hp), stream_of(stream), in, n, partials, out));
+  });
 }
 
 int f4s_vector_add_f32(f4s_hotpath* hp, uint64_t stream, uint64_t a, uint64_t b, uint64_t c, int32_t n) {
