@@ -146,6 +146,9 @@ def main() -> None:
     ap.add_argument("--cpu-sample-log2", type=int, default=28)
     ap.add_argument("--e2e-max-log2", type=int, default=30,
                     help="cap on the per-rank host sample of each array in the e2e leg (pinned host memory)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--profile", default=None,
+                    help="profiling mode: run one kernel (or 'all') a few times on a small case and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -177,6 +180,10 @@ def main() -> None:
 
     import flight4s_b200 as f4s
     from flight4s_b200.sharded import ShardedReducer
+
+    if args.profile:
+        profile_run(args.profile)
+        return
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -261,9 +268,12 @@ def main() -> None:
 
     # ---- e2e through the host-buffer public call
     e2e = None
-    try:
+    if args.e2e_steps <= 0:
+        e2e = {"value": None, "unit": "GB/s", "skipped": "--e2e-steps 0"}
+    else:
+      try:
         e2e = run_e2e(ctx, hp, red, x, xi, min(count, 1 << args.e2e_max_log2), world, dev, args.e2e_steps, barrier)
-    except Exception as exc:  # reported, not hidden
+      except Exception as exc:  # reported, not hidden
         e2e = {"value": None, "unit": "GB/s", "error": f"{type(exc).__name__}: {exc}"}
     del x, xi
     torch.cuda.empty_cache()
@@ -282,7 +292,7 @@ def main() -> None:
     per_launch_bytes = 4 * count
     achieved = per_launch_bytes / (kernel_ms[dominant] / 1e3) / 1e9
     traffic_per_elem = _traffic_table().get(dominant)
-    cpu = cpu_reference_run(1 << args.cpu_sample_log2, 3, 1, threads) if world == 1 else None
+    cpu = cpu_reference_run(1 << args.cpu_sample_log2, 3, 1, threads) if world == 1 and not args.no_cpu else None
     line = {
         "metric": "achieved HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -367,6 +377,87 @@ def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
             "api": "f4s_reduce_host (pinned host shard, chunked H2D overlapped with the reduction kernel)"}
 
 
+def profile_run(which: str) -> None:
+    """Small cases for ncu: each selected kernel 1 warm-up + 3 launches.
+    Inputs exceed L2 (126 MB) except the block sum, whose BASELINE size is
+    4 MiB; at most ~2.2 GB is on the device at once."""
+    import torch
+
+    import flight4s_b200 as f4s
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = f4s.CudaContext.open(0)
+    hp = ctx.hotpath()
+    want = (lambda k: True) if which == "all" else (lambda k: k == which)
+
+    def rep(fn):
+        for _ in range(4):
+            fn()
+        torch.cuda.synchronize()
+
+    n = 1 << 28
+    if any(want(k) for k in ("reduce_sum_f32", "reduce_argmax_f32", "reduce_sum_i32")):
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        hp.fill_synthetic(x, n, f4s.NORMAL_F32, seed=SEED)
+        out = torch.zeros(2, dtype=torch.int64, device=dev)
+        if want("reduce_sum_f32"):
+            rep(lambda: hp.reduce_into(f4s.REDUCE_SUM_F32, x, out))
+        if want("reduce_argmax_f32"):
+            rep(lambda: hp.reduce_into(f4s.REDUCE_ARGMAX_F32, x, out))
+        if want("reduce_sum_i32"):
+            hp.fill_synthetic(x, n, f4s.UNIFORM_I32, seed=SEED, ilo=-1000, ihi=1000)
+            rep(lambda: hp.reduce_into(f4s.REDUCE_SUM_I32, x, out))
+        del x
+    if want("vector_add_f32") or want("vector_add_bf16"):
+        m = 1 << 26
+        for dtype, kind, fn, key in [(torch.float32, f4s.UNIFORM_F32, hp.vector_add_f32, "vector_add_f32"),
+                                     (torch.bfloat16, f4s.UNIFORM_BF16, hp.vector_add_bf16, "vector_add_bf16")]:
+            if not want(key):
+                continue
+            a = torch.empty(m, dtype=dtype, device=dev)
+            b = torch.empty_like(a)
+            c = torch.empty_like(a)
+            hp.fill_synthetic(a, m, kind, seed=1)
+            hp.fill_synthetic(b, m, kind, seed=2)
+            rep(lambda: fn(a, b, c))
+            del a, b, c
+    if want("block_sum"):
+        m = 1 << 20
+        x = torch.empty(m, dtype=torch.float32, device=dev)
+        hp.fill_synthetic(x, m, f4s.UNIFORM_F32, seed=SEED)
+        parts = torch.empty(m // 256, dtype=torch.float32, device=dev)
+        o = torch.empty(1, dtype=torch.float32, device=dev)
+        ws = torch.zeros(hp.block_reduce_workspace_bytes(m), dtype=torch.uint8, device=dev)
+        rep(lambda: hp.block_reduce_sum_f32_into(x, parts, o, ws))
+    rows, cols = 8192, 8192
+    if want("softmax") or want("rmsnorm"):
+        xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)
+        yb = torch.empty_like(xb)
+        w = torch.empty(cols, dtype=torch.bfloat16, device=dev)
+        hp.fill_synthetic(xb, rows * cols, f4s.NORMAL_BF16, seed=SEED)
+        hp.fill_synthetic(w, cols, f4s.NORMAL_BF16, seed=SEED + 1, p0=1.0, p1=0.1)
+        if want("softmax"):
+            rep(lambda: hp.softmax_rows_bf16(xb, yb, rows, cols))
+        if want("rmsnorm"):
+            rep(lambda: hp.rmsnorm_rows_bf16(xb, w, yb, rows, cols, 1e-6))
+        del xb, yb
+    if want("fp8_quant") or want("fp8_dequant"):
+        m = rows * cols
+        xb = torch.empty(m, dtype=torch.bfloat16, device=dev)
+        hp.fill_synthetic(xb, m, f4s.NORMAL_BF16_OUTLIERS, seed=SEED, p0=0.0, p1=2.0, p2=1e-3, p3=50.0)
+        q = torch.empty(m, dtype=torch.uint8, device=dev)
+        s = torch.empty(m // 128, dtype=torch.float32, device=dev)
+        y = torch.empty_like(xb)
+        hp.fp8_quantize_e4m3(xb, q, s, rows, cols)
+        if want("fp8_quant"):
+            rep(lambda: hp.fp8_quantize_e4m3(xb, q, s, rows, cols))
+        if want("fp8_dequant"):
+            rep(lambda: hp.fp8_dequantize_e4m3(q, s, y, rows, cols))
+    torch.cuda.synchronize()
+    print(f"profile run done: {which}")
+    ctx.close()
+
+
 def kernel_table(ctx, hp, dev, peak) -> dict:
     """The other hot-path kernels at their BASELINE configurations, 1 GPU,
     CUDA events around `reps` back-to-back launches after warm-up."""
@@ -420,17 +511,34 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     parts = torch.empty(n // 256, dtype=torch.float32, device=dev)
     o = torch.empty(1, dtype=torch.float32, device=dev)
     ws = torch.zeros(hp.block_reduce_workspace_bytes(n), dtype=torch.uint8, device=dev)
-
-    class _W:
-        size_bytes = ws.numel()
-
-        @staticmethod
-        def data_ptr():
-            return ws.data_ptr()
-    fn = lambda: hp.block_reduce_sum_f32_into(x, parts, o, _W, stream=stream)  # noqa: E731
+    # A 4 MiB block sum runs for a few microseconds, less than one host-side
+    # launch through Python, so it is timed as CUDA-graph replays of
+    # back-to-back launches (device time per launch).
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    row("block_reduce_sum_f32 n=2^20 hot-L2", 4 * n + 4 * (n // 256), n, timeit(fn, reps=50))
-    row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, timeit(fn, reps=20, flush=flush))
+
+    def graph_ms(body, count):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            body()  # warm-up outside capture
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=side):
+                for _ in range(count):
+                    body()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / count
+
+    bs = lambda: hp.block_reduce_sum_f32_into(x, parts, o, ws, stream=torch.cuda.current_stream())  # noqa: E731
+    row("block_reduce_sum_f32 n=2^20 hot-L2", 4 * n + 4 * (n // 256), n, graph_ms(bs, 100), timing="cuda graph")
+    flushed = graph_ms(lambda: (flush.zero_(), bs()), 50) - graph_ms(lambda: flush.zero_(), 50)
+    row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, flushed, timing="cuda graph")
     del flush
 
     rows, cols = 32768, 8192

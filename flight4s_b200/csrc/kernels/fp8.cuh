@@ -29,8 +29,8 @@ namespace f4s {
 
 constexpr int kFp8Block = 128;
 constexpr int kFp8Threads = 256;
-constexpr int kQuantUnroll = 4;    // block pairs per warp per step
-constexpr int kDequantUnroll = 2;  // block quads per warp per step
+constexpr int kQuantUnroll = 4;    // 4-block steps in flight per warp
+constexpr int kDequantUnroll = 2;
 constexpr float kE4m3Max = 448.0f;
 constexpr float kFltMax = 3.402823466e38f;
 
@@ -57,53 +57,65 @@ __device__ __forceinline__ uint2 dequant_x4(uint32_t codes, float scale) {
 
 }  // namespace f4s
 
-// Flat vector quantizer: (x, codes, scales, num_blocks) with every block 128
-// contiguous elements.  A half-warp owns one block: each lane holds 8 bf16
-// (one 16-byte load), the amax is a 4-step xor shuffle inside the half-warp,
-// and each lane stores 8 codes (8 bytes).
-extern "C" __global__ void __launch_bounds__(f4s::kFp8Threads)
+// Flat vector kernels: every block is 128 contiguous elements (cols % 128
+// == 0), so the tensor is a flat run of blocks.  A quarter-warp (8 lanes)
+// owns one block and each lane 16 elements: the quantizer reads them with
+// one 256-bit load (32 bytes of bf16), takes the amax with 3 xor shuffles
+// inside the quarter-warp and stores 16 codes (16 bytes); the dequantizer
+// reads 16 codes and writes 32 bytes of bf16 with one 256-bit store.  A warp
+// covers 4 blocks per step and keeps kQuantUnroll / kDequantUnroll steps in
+// flight; the host launches enough warps that each runs its loop about once.
+// (minBlocksPerSM = 2 lets ptxas keep all four 32-byte loads in registers:
+// without it, it stops at 64 registers and spills.)
+extern "C" __global__ void __launch_bounds__(f4s::kFp8Threads, 2)
 f4s_fp8_quant_flat(const uint16_t* __restrict__ x, uint8_t* __restrict__ codes,
                    float* __restrict__ scales, int num_blocks) {
   using namespace f4s;
   const int lane = threadIdx.x % kWarp;
-  const int half = lane >> 4;         // which block of the pair
-  const int sub = lane & 15;          // 16-byte chunk within the block
+  const int quarter = lane >> 3;  // which block of the warp's four
+  const int sub = lane & 7;       // 16-element slice within the block
   const size_t warp_id = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarp;
   const size_t nwarps = static_cast<size_t>(gridDim.x) * blockDim.x / kWarp;
-  const size_t pairs = (static_cast<size_t>(num_blocks) + 1) / 2;
-  for (size_t p0 = warp_id; p0 < pairs; p0 += nwarps * kQuantUnroll) {
-    uint4 raw[kQuantUnroll];
+  const size_t quads = (static_cast<size_t>(num_blocks) + 3) / 4;
+  for (size_t q0 = warp_id; q0 < quads; q0 += nwarps * kQuantUnroll) {
+    u32x8 raw[kQuantUnroll];
     bool live[kQuantUnroll];
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
-      const size_t blk = 2 * (p0 + u * nwarps) + half;
-      live[u] = (p0 + u * nwarps) < pairs && blk < static_cast<size_t>(num_blocks);
-      raw[u] = live[u] ? ld_stream_u4(x + blk * kFp8Block + sub * 8) : make_uint4(0, 0, 0, 0);
+      const size_t blk = 4 * (q0 + u * nwarps) + quarter;
+      live[u] = (q0 + u * nwarps) < quads && blk < static_cast<size_t>(num_blocks);
+      if (live[u]) {
+        raw[u] = ld_stream_v8(x + blk * kFp8Block + sub * 16);
+      } else {
+        raw[u].lo = make_uint4(0, 0, 0, 0);
+        raw[u].hi = raw[u].lo;
+      }
     }
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
+      const uint32_t w[8] = {raw[u].lo.x, raw[u].lo.y, raw[u].lo.z, raw[u].lo.w,
+                             raw[u].hi.x, raw[u].hi.y, raw[u].hi.z, raw[u].hi.w};
       float amax = 0.0f;
-      amax = abs_max_bf16x2(amax, raw[u].x);
-      amax = abs_max_bf16x2(amax, raw[u].y);
-      amax = abs_max_bf16x2(amax, raw[u].z);
-      amax = abs_max_bf16x2(amax, raw[u].w);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      for (int j = 0; j < 8; ++j) amax = abs_max_bf16x2(amax, w[j]);
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       float scale, inv;
       block_scale(amax, scale, inv);
       if (live[u]) {
-        const size_t blk = 2 * (p0 + u * nwarps) + half;
-        const uint32_t q0 = quant_bf16x2(raw[u].x, inv) | (quant_bf16x2(raw[u].y, inv) << 16);
-        const uint32_t q1 = quant_bf16x2(raw[u].z, inv) | (quant_bf16x2(raw[u].w, inv) << 16);
-        st_stream_u2(codes + blk * kFp8Block + sub * 8, make_uint2(q0, q1));
+        const size_t blk = 4 * (q0 + u * nwarps) + quarter;
+        uint4 q;
+        q.x = quant_bf16x2(w[0], inv) | (quant_bf16x2(w[1], inv) << 16);
+        q.y = quant_bf16x2(w[2], inv) | (quant_bf16x2(w[3], inv) << 16);
+        q.z = quant_bf16x2(w[4], inv) | (quant_bf16x2(w[5], inv) << 16);
+        q.w = quant_bf16x2(w[6], inv) | (quant_bf16x2(w[7], inv) << 16);
+        st_stream_u4(codes + blk * kFp8Block + sub * 16, q);
         if (sub == 0) scales[blk] = scale;
       }
     }
   }
 }
 
-// Flat vector dequantizer: (codes, scales, y, num_blocks).  Eight lanes own
-// one block: each lane loads 16 codes (16 bytes) and stores 16 bf16 (32 bytes).
 extern "C" __global__ void __launch_bounds__(f4s::kFp8Threads)
 f4s_fp8_dequant_flat(const uint8_t* __restrict__ codes, const float* __restrict__ scales,
                      uint16_t* __restrict__ y, int num_blocks) {
@@ -133,9 +145,10 @@ f4s_fp8_dequant_flat(const uint8_t* __restrict__ codes, const float* __restrict_
         const uint2 b = dequant_x4(raw[u].y, sc[u]);
         const uint2 c = dequant_x4(raw[u].z, sc[u]);
         const uint2 d = dequant_x4(raw[u].w, sc[u]);
-        uint4* dst = reinterpret_cast<uint4*>(y + blk * kFp8Block + sub * 16);
-        st_stream_u4(dst, make_uint4(a.x, a.y, b.x, b.y));
-        st_stream_u4(dst + 1, make_uint4(c.x, c.y, d.x, d.y));
+        u32x8 o;
+        o.lo = make_uint4(a.x, a.y, b.x, b.y);
+        o.hi = make_uint4(c.x, c.y, d.x, d.y);
+        st_stream_v8(y + blk * kFp8Block + sub * 16, o);
       }
     }
   }

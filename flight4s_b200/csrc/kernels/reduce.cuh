@@ -134,13 +134,15 @@ struct ArgmaxF32Op {
   struct Thread {
     int32_t vkey = INT32_MIN;  // best key seen in the vector body
     uint64_t best_vec = UINT64_MAX;
+    float4 best = make_float4(0.f, 0.f, 0.f, 0.f);  // that vector's values
     ArgmaxPartial s{INT32_MIN, INT64_MAX};  // scalar head/tail candidate
   };
   static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t base,
                                               uint64_t stride, int count) {
-    // The hot loop tracks only the best vector; the lane inside it is
-    // resolved once at the end.  Vectors arrive in increasing index order,
-    // so a strict '>' keeps the lowest index.
+    // The hot loop tracks only the best vector (kept in registers; the
+    // update branch is rarely taken); the lane inside it is resolved once
+    // at the end.  Vectors arrive in increasing index order, so a strict
+    // '>' keeps the lowest index.
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
       if (u < count) {
@@ -150,6 +152,7 @@ struct ArgmaxF32Op {
         if (k > t.vkey) {
           t.vkey = k;
           t.best_vec = base + u * stride;
+          t.best = v[u];
         }
       }
     }
@@ -160,8 +163,7 @@ struct ArgmaxF32Op {
   static __device__ __forceinline__ Partial finish(Thread& t, const float* in, uint64_t head) {
     ArgmaxPartial p = t.s;
     if (t.best_vec != UINT64_MAX) {
-      // One re-read of the winning vector (an L2 hit) finds its lowest lane.
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(in + head) + t.best_vec);
+      const float4 v = t.best;
       int lane = 3;
       if (total_order_key(v.z) == t.vkey) lane = 2;
       if (total_order_key(v.y) == t.vkey) lane = 1;

@@ -9,9 +9,11 @@
 //   softmax: y = bf16_rn( exp(x - max) * (1 / sum exp(x - max)) )
 //   rmsnorm: y = bf16_rn( (x * rsqrt(mean(x^2) + eps)) * w )
 //
-// B200 mapping: one 256-thread CTA per row; a row of up to 256*8*VPT bf16
+// B200 mapping: a 256-thread CTA per row; a row of up to 256*8*VPT bf16
 // lives in registers (VPT 16-byte vectors per thread), so HBM sees exactly
-// one read and one write per element.  Row reductions are warp shuffles plus
+// one read and one write per element.  Softmax launches one CTA per row;
+// RMSNorm uses persistent CTAs that keep the weight slice in registers and
+// prefetch their next row.  Row reductions are warp shuffles plus
 // one shared-memory exchange.  Rows that are not a multiple of 8 elements
 // wide, or too wide for registers, use a looped kernel that re-reads the row
 // (from L2 for realistic widths) with the same arithmetic.
@@ -117,20 +119,63 @@ __device__ __forceinline__ void softmax_row_regs(const uint16_t* in, uint16_t* o
 }
 
 template <int VPT>
-__device__ __forceinline__ void rmsnorm_row_regs(const uint16_t* in, const float (&w)[VPT * 8],
-                                                 uint16_t* out, int cols, float eps, float* red) {
+__device__ __forceinline__ void load_row_raw(const uint16_t* row, int nvec, uint4 (&raw)[VPT]) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = threadIdx.x + k * kRowBlock;
+    raw[k] = v < nvec ? ld_stream_u4(reinterpret_cast<const uint4*>(row) + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// RMSNorm over the rows blockIdx.x, blockIdx.x + gridDim.x, ...: the weight
+// slice and the current row stay packed (bf16 pairs) in registers, and the
+// next row's loads are issued before the current row's reduction, so a CTA
+// keeps a row of loads in flight across its barrier.
+template <int VPT>
+__device__ __forceinline__ void rmsnorm_rows_packed(const uint16_t* __restrict__ in,
+                                                    const uint16_t* __restrict__ weight,
+                                                    uint16_t* __restrict__ out, int rows, int cols, float eps) {
+  __shared__ float red[2][kRowWarps];
   const int nvec = cols / 8;
-  float x[VPT * 8];
-  bool valid[VPT];
-  load_row<VPT>(in, nvec, x, valid);
-  float ss = 0.0f;
+  uint4 w[VPT], cur[VPT], nxt[VPT];
+  load_row_raw<VPT>(weight, nvec, w);
+  int r = blockIdx.x;
+  if (r < rows) load_row_raw<VPT>(in + static_cast<size_t>(r) * cols, nvec, cur);
+  int parity = 0;
+  for (; r < rows; r += gridDim.x) {
+    const int next = r + gridDim.x;
+    if (next < rows) load_row_raw<VPT>(in + static_cast<size_t>(next) * cols, nvec, nxt);
+    float ss = 0.0f;
 #pragma unroll
-  for (int k = 0; k < VPT * 8; ++k) ss = fmaf(x[k], x[k], ss);
-  ss = block_sum(ss, red);
-  const float r = rsqrtf(ss / static_cast<float>(cols) + eps);
+    for (int k = 0; k < VPT; ++k) {
+      const uint32_t q[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
 #pragma unroll
-  for (int k = 0; k < VPT * 8; ++k) x[k] = (x[k] * r) * w[k];
-  store_row<VPT>(out, x, valid);
+      for (int j = 0; j < 4; ++j) {
+        const float a = bf16_lo(q[j]), b = bf16_hi(q[j]);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+      }
+    }
+    ss = block_sum(ss, red[parity]);
+    parity ^= 1;
+    const float rs = rsqrtf(ss / static_cast<float>(cols) + eps);
+    uint4* o = reinterpret_cast<uint4*>(out + static_cast<size_t>(r) * cols);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = threadIdx.x + k * kRowBlock;
+      if (v < nvec) {
+        const uint32_t q[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
+        const uint32_t ww[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+        uint32_t y[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          y[j] = pack_bf16x2_rn((bf16_lo(q[j]) * rs) * bf16_lo(ww[j]), (bf16_hi(q[j]) * rs) * bf16_hi(ww[j]));
+        st_stream_u4(o + v, make_uint4(y[0], y[1], y[2], y[3]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) cur[k] = nxt[k];
+  }
 }
 
 }  // namespace f4s
@@ -155,23 +200,12 @@ F4S_SOFTMAX_REGS(8)
 #undef F4S_SOFTMAX_REGS
 
 // (in, weight, out, rows, cols, eps); cols % 8 == 0 and cols <= 2048 * VPT.
-// The weight slice of each thread is loaded once and stays in registers
-// while the CTA strides over rows.
-#define F4S_RMSNORM_REGS(VPT)                                                                \
-  extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)                                \
-      f4s_rmsnorm_rows_bf16_v##VPT(const uint16_t* __restrict__ in,                            \
-                                   const uint16_t* __restrict__ weight,                        \
-                                   uint16_t* __restrict__ out, int rows, int cols, float eps) { \
-    __shared__ float red[2][f4s::kRowWarps];                                                   \
-    float w[VPT * 8];                                                                          \
-    bool valid[VPT];                                                                           \
-    f4s::load_row<VPT>(weight, cols / 8, w, valid);                                            \
-    int parity = 0;                                                                            \
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {                                       \
-      f4s::rmsnorm_row_regs<VPT>(in + static_cast<size_t>(r) * cols, w,                       \
-                                 out + static_cast<size_t>(r) * cols, cols, eps, red[parity]); \
-      parity ^= 1;                                                                             \
-    }                                                                                          \
+#define F4S_RMSNORM_REGS(VPT)                                                                 \
+  extern "C" __global__ void __launch_bounds__(f4s::kRowBlock)                                 \
+      f4s_rmsnorm_rows_bf16_v##VPT(const uint16_t* __restrict__ in,                             \
+                                   const uint16_t* __restrict__ weight,                         \
+                                   uint16_t* __restrict__ out, int rows, int cols, float eps) {  \
+    f4s::rmsnorm_rows_packed<VPT>(in, weight, out, rows, cols, eps);                            \
   }
 F4S_RMSNORM_REGS(1)
 F4S_RMSNORM_REGS(2)

@@ -16,6 +16,7 @@ namespace {
 // Launch constants shared with the kernels (csrc/kernels/*.cuh).
 constexpr int kReduceBlock = 512;
 constexpr int kReduceUnroll = 8;
+constexpr int kReduceWaves = 8;
 constexpr std::uint64_t kReducePartialOffset = 256;
 constexpr std::uint64_t kReducePartialBytes = 16;
 constexpr int kBlockSumThreads = 1024;
@@ -25,6 +26,8 @@ constexpr int kAddBlock = 256;
 constexpr int kRowBlock = 256;
 constexpr int kFp8Threads = 256;
 constexpr int kFp8Block = 128;
+constexpr int kQuantUnroll = 4;
+constexpr int kDequantUnroll = 2;
 
 void check(CUresult r, const char* what) {
   if (r != CUDA_SUCCESS) {
@@ -140,9 +143,9 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
 }
 
 std::uint64_t Hotpath::reduce_workspace_bytes() const {
-  // One partial slot per co-resident CTA bounds every cluster size: at most
-  // 2048 / kReduceBlock CTAs fit on an SM.
-  const std::uint64_t ctas = static_cast<std::uint64_t>(sm_count_) * (2048 / kReduceBlock);
+  // One partial slot per launched cluster; kReduceWaves waves of at most
+  // 2048 / kReduceBlock co-resident CTAs per SM bound every cluster size.
+  const std::uint64_t ctas = static_cast<std::uint64_t>(sm_count_) * (2048 / kReduceBlock) * kReduceWaves;
   return kReducePartialOffset + kReducePartialBytes * ctas;
 }
 
@@ -173,10 +176,13 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
   if (op == ReduceOp::kSumF32 && out % 8 != 0) throw std::invalid_argument("f64 output must be 8-byte aligned");
   if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
   const int cluster = shape_.reduce_cluster;
-  // Enough clusters to give each thread >= one unrolled step, at most one wave.
+  // Enough clusters to give each thread >= one unrolled step, at most
+  // kReduceWaves waves of co-resident clusters (several waves measured
+  // faster than one persistent wave: no idle tail).
   const std::uint64_t per_cluster = static_cast<std::uint64_t>(cluster) * kReduceBlock * 4 * kReduceUnroll;
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
-  const int clusters = static_cast<int>(std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters)));
+  const int clusters = static_cast<int>(
+      std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters) * kReduceWaves));
   const std::uint64_t need = kReducePartialOffset + kReducePartialBytes * static_cast<std::uint64_t>(clusters);
   if (workspace_bytes < need) {
     throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
@@ -227,8 +233,9 @@ CUresult Hotpath::vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdevice
   const std::uint64_t elem = bf16 ? 2 : 4;
   if (a % elem != 0 || b % elem != 0 || c % elem != 0)
     throw std::invalid_argument("vectorAdd buffers must be aligned to their element size");
-  const std::int64_t per_cta = static_cast<std::int64_t>(kAddBlock) * (bf16 ? 8 : 4);
-  const int grid = static_cast<int>(std::min<std::int64_t>(shape_.add_grid, (n + per_cta - 1) / per_cta));
+  // one thread per 32-byte vector (the kernel loops for any other grid)
+  const std::int64_t per_cta = static_cast<std::int64_t>(kAddBlock) * (bf16 ? 16 : 8);
+  const int grid = static_cast<int>((n + per_cta - 1) / per_cta);
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
@@ -268,7 +275,9 @@ CUresult Hotpath::softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out,
     if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
       per_sm = blocks;
   }
-  const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * per_sm * 8));
+  // one CTA per row (measured best: no persistent tail)
+  (void)per_sm;
+  const int grid = rows;
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
@@ -297,8 +306,10 @@ CUresult Hotpath::rmsnorm_rows(CUstream stream, CUdeviceptr in, CUdeviceptr weig
     if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
       per_sm = blocks;
   }
-  // Persistent: one wave of CTAs, each keeps its weight slice in registers.
-  const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * per_sm));
+  // Persistent CTAs (8 per SM, measured flat between 2 and 8 for 8192-wide
+  // rows), each keeping its weight slice in registers across its rows.
+  (void)per_sm;
+  const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * 8));
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
@@ -318,13 +329,15 @@ CUresult Hotpath::fp8_quantize(CUstream stream, CUdeviceptr x, CUdeviceptr codes
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   const std::int64_t total = static_cast<std::int64_t>(rows) * cols;
-  if (cols % kFp8Block == 0 && x % 16 == 0 && codes % 8 == 0 && total / kFp8Block <= INT32_MAX) {
+  if (cols % kFp8Block == 0 && x % 32 == 0 && codes % 16 == 0 && total / kFp8Block <= INT32_MAX) {
+    // one warp per kQuantUnroll 4-block steps: the loop runs about once
     const std::int64_t blocks = total / kFp8Block;
-    const std::int64_t ctas = (blocks / 2 + kFp8Threads / 32 - 1) / (kFp8Threads / 32) + 1;
+    const std::int64_t warps = (blocks + 4 * kQuantUnroll - 1) / (4 * kQuantUnroll);
+    const std::int64_t ctas = (warps + kFp8Threads / 32 - 1) / (kFp8Threads / 32);
     ArgumentPack args;
     args.ptr(x).ptr(codes).ptr(scales).i32(static_cast<std::int32_t>(blocks));
-    return cur.finish(launch(function("f4s_fp8_quant_flat"), stream,
-                             static_cast<int>(std::min<std::int64_t>(shape_.fp8_grid, ctas)), kFp8Threads, 0, args));
+    return cur.finish(launch(function("f4s_fp8_quant_flat"), stream, static_cast<int>(std::max<std::int64_t>(ctas, 1)),
+                             kFp8Threads, 0, args));
   }
   ArgumentPack args;
   args.ptr(x).ptr(codes).ptr(scales).i32(rows).i32(cols);
@@ -343,13 +356,14 @@ CUresult Hotpath::fp8_dequantize(CUstream stream, CUdeviceptr codes, CUdeviceptr
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   const std::int64_t total = static_cast<std::int64_t>(rows) * cols;
-  if (cols % kFp8Block == 0 && codes % 16 == 0 && y % 16 == 0 && total / kFp8Block <= INT32_MAX) {
+  if (cols % kFp8Block == 0 && codes % 16 == 0 && y % 32 == 0 && total / kFp8Block <= INT32_MAX) {
     const std::int64_t blocks = total / kFp8Block;
-    const std::int64_t ctas = (blocks / 4 + kFp8Threads / 32 - 1) / (kFp8Threads / 32) + 1;
+    const std::int64_t warps = (blocks + 4 * kDequantUnroll - 1) / (4 * kDequantUnroll);
+    const std::int64_t ctas = (warps + kFp8Threads / 32 - 1) / (kFp8Threads / 32);
     ArgumentPack args;
     args.ptr(codes).ptr(scales).ptr(y).i32(static_cast<std::int32_t>(blocks));
     return cur.finish(launch(function("f4s_fp8_dequant_flat"), stream,
-                             static_cast<int>(std::min<std::int64_t>(shape_.fp8_grid, ctas)), kFp8Threads, 0, args));
+                             static_cast<int>(std::max<std::int64_t>(ctas, 1)), kFp8Threads, 0, args));
   }
   ArgumentPack args;
   args.ptr(codes).ptr(scales).ptr(y).i32(rows).i32(cols);

@@ -34,6 +34,15 @@ def _count(x: Any, n: Optional[int]) -> int:
     raise ValueError("element count required for a raw device address")
 
 
+def _nbytes(buf: Any) -> int:
+    """Byte size of a CudaDeviceBuffer, a torch tensor or an object with size_bytes."""
+    if hasattr(buf, "size_bytes"):
+        return int(buf.size_bytes)
+    if hasattr(buf, "numel") and hasattr(buf, "element_size"):
+        return int(buf.numel() * buf.element_size())
+    raise ValueError("buffer size unknown: pass a CudaDeviceBuffer or a torch tensor")
+
+
 def unpack_argmax_key(packed: int) -> tuple[float, int]:
     """(value, index) of a packed argmax key:
     (signed totalOrder key << 32) | (0xFFFFFFFF - index)."""
@@ -93,7 +102,7 @@ class Hotpath:
     def reduce_into(self, op: int, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
                     accumulate: bool = False, index_base: int = 0, workspace: Any = None) -> None:
         ws = self.workspace() if workspace is None else workspace
-        ws_bytes = ws.size_bytes if hasattr(ws, "size_bytes") else self.workspace_bytes
+        ws_bytes = _nbytes(ws)
         args = (self._h, stream_handle(stream), device_address(x), _count(x, n), device_address(out),
                 device_address(ws), ws_bytes)
         if op == REDUCE_SUM_F32:
@@ -135,7 +144,7 @@ class Hotpath:
         out = np.zeros(2, np.uint64)
         host = np.ascontiguousarray(host)
         check(lib.f4s_reduce_host(self._h, op, host.ctypes.data, host.size, index_base, out.ctypes.data,
-                                  device_address(staging), staging.size_bytes, device_address(ws), ws.size_bytes,
+                                  device_address(staging), _nbytes(staging), device_address(ws), _nbytes(ws),
                                   stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")
         return out
 
@@ -148,7 +157,7 @@ class Hotpath:
                                   stream: Any = None) -> None:
         check(lib.f4s_block_reduce_sum_f32(self._h, stream_handle(stream), device_address(x), _count(x, n),
                                            device_address(partials), device_address(out),
-                                           device_address(workspace), workspace.size_bytes),
+                                           device_address(workspace), _nbytes(workspace)),
               "block_reduce_sum_f32")
 
     # ---------------------------------------------------------- elementwise

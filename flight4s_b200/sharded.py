@@ -71,7 +71,7 @@ class ShardedReducer:
         if shard.numel() != self.count:
             raise ValueError(f"rank {self.rank} shard holds {shard.numel()} elements, expected {self.count}")
         self.hp.reduce_into(op, shard, out, n=self.count, stream=stream, index_base=self.offset,
-                            workspace=_Workspace(self.workspace))
+                            workspace=self.workspace)
 
     def sum_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
         self._reduce(REDUCE_SUM_F32, shard, self.f64, stream)
@@ -99,17 +99,6 @@ class ShardedReducer:
         if packed == -(1 << 63):
             return float("nan"), -1
         return unpack_argmax_key(packed)
-
-
-class _Workspace:
-    """Adapter: a torch uint8 tensor used as the reduction workspace."""
-
-    def __init__(self, t: torch.Tensor):
-        self.t = t
-        self.size_bytes = t.numel()
-
-    def data_ptr(self) -> int:
-        return self.t.data_ptr()
 
 
 def cpu_sharded_combine(partial_fn: Callable[[int, int, int], tuple[float, int, int]], n_total: int) -> tuple:
