@@ -62,6 +62,20 @@ def _traffic_table() -> dict:
     return out
 
 
+class _stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration of the block."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
 # --------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, gpus: str):
@@ -188,7 +202,12 @@ def main() -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300))
+        # NCCL may print a version banner on stdout while the communicator
+        # comes up; keep stdout for the one JSON line.
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300))
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
     ctx = f4s.CudaContext.open(local)
     hp = ctx.hotpath()
     red = ShardedReducer(hp, dev, N_TOTAL)
@@ -212,6 +231,7 @@ def main() -> None:
     for _ in range(args.warmup):
         for _, op in ops:
             op()
+    red.wait()
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     sampler = ClockSampler(visible if visible else ",".join(str(i) for i in range(world))) if rank == 0 else None
     torch.cuda.synchronize()
@@ -230,6 +250,7 @@ def main() -> None:
             op()
             b.record(stream)
             kev[name].append((a, b))
+    red.wait(stream)  # the last collectives belong to the timed region
     end.record(stream)
     torch.cuda.synchronize()
     t_host1 = time.time()
@@ -243,11 +264,12 @@ def main() -> None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_total = float(ms_t.item())
     ms_step = ms_total / args.steps
-    # per-kernel average (each interval spans the kernel plus, for N > 1, its all_reduce;
-    # the kernel alone is timed at N = 1 and in the table below)
+    # per-kernel average: events on the compute stream bracket the kernel
+    # (for N > 1 the all_reduce runs on NCCL's stream, overlapping the next kernel)
     kernel_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / len(evs) for name, evs in kev.items()}
 
     # results of the last step (checked against torch on the full array at N = 1)
+    red.wait()
     s_val = float(red.f64.item())
     i_val = int(red.i32.item())
     v_max, i_max = ShardedReducer.argmax_result(red.arg)
@@ -272,7 +294,9 @@ def main() -> None:
         e2e = {"value": None, "unit": "GB/s", "skipped": "--e2e-steps 0"}
     else:
       try:
-        e2e = run_e2e(ctx, hp, red, x, xi, min(count, 1 << args.e2e_max_log2), world, dev, args.e2e_steps, barrier)
+        # pinned host sample per rank, capped so all ranks together pin at most 2^e2e_max_log2 x 8 bytes
+        e2e_count = min(count, (1 << args.e2e_max_log2) // world)
+        e2e = run_e2e(ctx, hp, red, x, xi, e2e_count, world, dev, args.e2e_steps, barrier)
       except Exception as exc:  # reported, not hidden
         e2e = {"value": None, "unit": "GB/s", "error": f"{type(exc).__name__}: {exc}"}
     del x, xi
@@ -306,8 +330,7 @@ def main() -> None:
                      else "fallback 6.65 TB/s", "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (traffic_per_elem * count) if traffic_per_elem else None,
                      "algorithmic_bytes_per_launch": per_launch_bytes,
-                     "kernel_ms": kernel_ms if world == 1 else None,
-                     "interval_ms_incl_allreduce": kernel_ms if world > 1 else None},
+                     "kernel_ms": kernel_ms},
         "results": {"sum_f32": s_val, "sum_i32": i_val, "max_f32": v_max, "argmax": i_max, "verified_vs_torch": verified},
         "gpu_launches": 3 * args.steps * world,
         "clocks": clocks,

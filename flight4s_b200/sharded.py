@@ -15,6 +15,7 @@ torch.distributed (NCCL over NVLink on GPUs; gloo in the CPU tests, where
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Any, Callable, Optional
 
 import torch
@@ -51,8 +52,14 @@ def combine_argmax(packed: torch.Tensor, group: Any = None) -> torch.Tensor:
 
 
 class ShardedReducer:
-    """Per-rank reduction + one all_reduce.  Buffers are device tensors
-    allocated once; `*_async` methods only enqueue work on `stream`."""
+    """Per-rank reduction + one all_reduce per op.
+
+    `*_async` methods enqueue the kernel on `stream` and start the
+    all_reduce asynchronously, so the collective of one op overlaps the
+    kernel of the next (the three reductions are independent).  Each op has
+    its own partial buffer; before a kernel overwrites it, the stream waits
+    for that buffer's previous all_reduce.  Call `wait()` (device-side) before
+    reading results on `stream`; the `*_result` helpers do so."""
 
     def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None):
         self.hp = hotpath
@@ -66,32 +73,69 @@ class ShardedReducer:
         self.i32 = torch.zeros(1, dtype=torch.int32, device=device)
         self.arg = torch.zeros(2, dtype=torch.int64, device=device)
         self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
+        self._pending: dict[int, Any] = {}
+
+    @staticmethod
+    def _on(stream: Optional[torch.cuda.Stream]):
+        """Make `stream` torch's current stream: torch orders collectives and
+        Work.wait() against the current stream."""
+        return torch.cuda.stream(stream) if isinstance(stream, torch.cuda.Stream) else contextlib.nullcontext()
 
     def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
         if shard.numel() != self.count:
             raise ValueError(f"rank {self.rank} shard holds {shard.numel()} elements, expected {self.count}")
-        self.hp.reduce_into(op, shard, out, n=self.count, stream=stream, index_base=self.offset,
-                            workspace=self.workspace)
+        prior = self._pending.pop(op, None)
+        if prior is not None:
+            with self._on(stream):
+                prior.wait()  # the stream waits until that all_reduce has released `out`
+        self.hp.reduce_into(op, shard, out, n=self.count,
+                            stream=stream if stream is not None else torch.cuda.current_stream(),
+                            index_base=self.offset, workspace=self.workspace)
+
+    def _combine(self, op: int, tensor: torch.Tensor, reduce_op, stream: Optional[torch.cuda.Stream]) -> None:
+        if self.world > 1:
+            with self._on(stream):
+                self._pending[op] = dist.all_reduce(tensor, op=reduce_op, group=self.group, async_op=True)
+
+    def wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Make `stream` (default: the current stream) wait for every
+        outstanding all_reduce."""
+        with self._on(stream):
+            for work in self._pending.values():
+                work.wait()
+        self._pending.clear()
 
     def sum_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
         self._reduce(REDUCE_SUM_F32, shard, self.f64, stream)
-        if self.world > 1:
-            combine_sum_f64(self.f64, self.group)
+        self._combine(REDUCE_SUM_F32, self.f64, dist.ReduceOp.SUM, stream)
         return self.f64
 
     def sum_i32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
         self._reduce(REDUCE_SUM_I32, shard, self.i32, stream)
-        if self.world > 1:
-            combine_sum_i32(self.i32, self.group)
+        self._combine(REDUCE_SUM_I32, self.i32, dist.ReduceOp.SUM, stream)
         return self.i32
 
     def argmax_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
         if self.n_total - 1 > MAX_PACKED_INDEX:
             raise ValueError("sharded argmax packs 32-bit global indices: n_total must be <= 2^32")
         self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
-        if self.world > 1:
-            combine_argmax(self.arg[:1], self.group)
+        self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
         return self.arg
+
+    def sum_f32(self, shard: torch.Tensor, stream=None) -> float:
+        self.sum_f32_async(shard, stream)
+        self.wait(stream)
+        return float(self.f64.item())
+
+    def sum_i32(self, shard: torch.Tensor, stream=None) -> int:
+        self.sum_i32_async(shard, stream)
+        self.wait(stream)
+        return int(self.i32.item())
+
+    def argmax_f32(self, shard: torch.Tensor, stream=None) -> tuple[float, int]:
+        self.argmax_f32_async(shard, stream)
+        self.wait(stream)
+        return self.argmax_result(self.arg)
 
     @staticmethod
     def argmax_result(arg: torch.Tensor) -> tuple[float, int]:

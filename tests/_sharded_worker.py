@@ -1,0 +1,51 @@
+"""torchrun worker for tests/test_gpu_sharded.py: sharded reductions over
+the ranks' GPUs, results written by rank 0 as JSON to argv[1]."""
+import json
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch
+import torch.distributed as dist
+
+import flight4s_b200 as f4s
+from flight4s_b200.sharded import ShardedReducer
+
+
+def main() -> None:
+    out_path = sys.argv[1]
+    n_total = int(sys.argv[2])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    ctx = f4s.CudaContext.open(local)
+    hp = ctx.hotpath()
+    red = ShardedReducer(hp, dev, n_total)
+    x = torch.empty(max(red.count, 1), dtype=torch.float32, device=dev)
+    xi = torch.empty(max(red.count, 1), dtype=torch.int32, device=dev)
+    hp.fill_synthetic(x, red.count, f4s.UNIFORM_F32, seed=99, offset=red.offset)
+    hp.fill_synthetic(xi, red.count, f4s.UNIFORM_I32, seed=99, offset=red.offset, ilo=-1000, ihi=1000)
+    xs, xis = x[:red.count], xi[:red.count]
+    results = []
+    for _ in range(2):  # twice: workspaces and outputs are reused
+        red.sum_f32_async(xs)  # three collectives in flight at once
+        red.sum_i32_async(xis)
+        red.argmax_f32_async(xs)
+        red.wait()
+        s, i, packed = float(red.f64.item()), int(red.i32.item()), int(red.arg[0].item())
+        assert red.sum_i32(xis) == i and red.argmax_f32(xs)[1] >= 0 and red.sum_f32(xs) == s
+        results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed})
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local])
+    if dist.get_rank() == 0:
+        Path(out_path).write_text(json.dumps({"world": dist.get_world_size(), "results": results}))
+    ctx.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,53 @@
+"""Sharded full-array reductions over 2 GPUs of one node (one process per
+GPU, NCCL all_reduce of the per-GPU partials) against the whole-array
+oracle.  Skipped when fewer than 2 GPUs are visible."""
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+HERE = Path(__file__).resolve().parent
+
+
+def _gpus() -> int:
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("n_total", [(1 << 24) + 5, 3])
+def test_two_gpu_sharded_reductions_match_oracle(tmp_path, n_total):
+    out = tmp_path / "result.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", str(HERE / "_sharded_worker.py"), str(out),
+           str(n_total)]
+    proc = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    got = json.loads(out.read_text())
+    assert got["world"] == 2
+    x = orc.uniform_f32(n_total, seed=99)
+    xi = orc.uniform_i32(n_total, seed=99, lo=-1000, hi=1000)
+    exact, abs_sum = orc.sum_f32_exact(x)
+    v, idx = orc.argmax_f32(x)
+    for r in got["results"]:
+        assert abs(r["sum_f32"] - exact) <= 1e-5 * abs_sum
+        assert r["sum_i32"] == orc.sum_i32(xi)
+        assert r["argmax_packed"] == orc.argmax_packed_key(v, idx)
