@@ -407,6 +407,17 @@ int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n
   });
 }
 
+int f4s_reduce_host_sum_argmax_f32(f4s_hotpath* hp, const void* host_in, uint64_t n, uint64_t index_base,
+                                   void* host_sum_out, void* host_argmax_out, uint64_t staging,
+                                   uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes, uint64_t copy_stream,
+                                   uint64_t compute_stream) {
+  return guarded([&] {
+    return op_status(hot(hp).reduce_host_sum_argmax(host_in, n, index_base, host_sum_out, host_argmax_out, staging,
+                                                    staging_bytes, ws, ws_bytes, stream_of(copy_stream),
+                                                    stream_of(compute_stream)));
+  });
+}
+
 uint64_t f4s_block_reduce_workspace_bytes(int32_t n) {
   return Hotpath::block_sum_workspace_bytes(n < 0 ? 0 : n);
 }

@@ -391,22 +391,45 @@ CUresult Hotpath::fill_synthetic(CUstream stream, CUdeviceptr out, std::uint64_t
 }
 
 CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n, std::uint64_t index_base,
-                              void* host_out,
-                              CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
-                              std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream) {
+                              void* host_out, CUdeviceptr staging, std::uint64_t staging_bytes,
+                              CUdeviceptr workspace, std::uint64_t workspace_bytes, CUstream copy_stream,
+                              CUstream compute_stream) {
+  void* outs[1] = {host_out};
+  return reduce_host_ops(&op, 1, host_in, n, index_base, outs, staging, staging_bytes, workspace, workspace_bytes,
+                         copy_stream, compute_stream);
+}
+
+CUresult Hotpath::reduce_host_sum_argmax(const void* host_in, std::uint64_t n, std::uint64_t index_base,
+                                         void* host_sum_out, void* host_argmax_out, CUdeviceptr staging,
+                                         std::uint64_t staging_bytes, CUdeviceptr workspace,
+                                         std::uint64_t workspace_bytes, CUstream copy_stream,
+                                         CUstream compute_stream) {
+  const ReduceOp ops[2] = {ReduceOp::kSumF32, ReduceOp::kArgmaxF32};
+  void* outs[2] = {host_sum_out, host_argmax_out};
+  return reduce_host_ops(ops, 2, host_in, n, index_base, outs, staging, staging_bytes, workspace, workspace_bytes,
+                         copy_stream, compute_stream);
+}
+
+CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* host_in, std::uint64_t n,
+                                  std::uint64_t index_base, void* const* host_outs, CUdeviceptr staging,
+                                  std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
+                                  CUstream copy_stream, CUstream compute_stream) {
   if (n > 0 && host_in == nullptr) throw std::invalid_argument("host input must not be null");
-  if (host_out == nullptr) throw std::invalid_argument("host output must not be null");
+  for (int i = 0; i < nops; ++i)
+    if (host_outs[i] == nullptr) throw std::invalid_argument("host output must not be null");
   require_ptr(staging, "staging buffer");
   if (staging % 256 != 0) throw std::invalid_argument("staging buffer must be 256-byte aligned");
   if (copy_stream == nullptr || compute_stream == nullptr || copy_stream == compute_stream)
-    throw std::invalid_argument("reduce_host needs two distinct non-null streams");
-  // staging = [256 B device-side result | buffer 0 | buffer 1]
+    throw std::invalid_argument("host-buffer reductions need two distinct non-null streams");
+  // staging = [256 B of device-side results (32 B per op) | buffer 0 | buffer 1]
   const std::uint64_t half = ((staging_bytes > 256 ? staging_bytes - 256 : 0) / 2) / 256 * 256;
   if (half < 256) throw std::invalid_argument("staging buffer too small (need >= 768 bytes)");
   const std::uint64_t chunk = half / 4;  // elements (4-byte types)
-  const CUdeviceptr result = staging;
   const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
-  const std::uint64_t out_bytes = op == ReduceOp::kSumF32 ? 8 : op == ReduceOp::kSumI32 ? 4 : 16;
+  auto result_slot = [&](int i) { return staging + 32 * static_cast<CUdeviceptr>(i); };
+  auto out_bytes = [](ReduceOp op) -> std::size_t {
+    return op == ReduceOp::kSumF32 ? 8 : op == ReduceOp::kSumI32 ? 4 : 16;
+  };
 
   const DriverApi& api = require_driver();
   Current cur(context_);
@@ -429,14 +452,15 @@ CUresult Hotpath::reduce_host(ReduceOp op, const void* host_in, std::uint64_t n,
                                 copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(copied[b], copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuStreamWaitEvent(compute_stream, copied[b], 0);
-    if (r == CUDA_SUCCESS) {
-      // Pushing the same context again inside reduce() is harmless.
-      r = reduce(op, compute_stream, buffers[b], count, result, workspace, workspace_bytes, index_base + first,
-                 k > 0 ? 1 : 0);
-    }
+    // every op reduces the same staged chunk (one transfer, nops kernels);
+    // pushing the same context again inside reduce() is harmless
+    for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
+      r = reduce(ops[i], compute_stream, buffers[b], count, result_slot(i), workspace, workspace_bytes,
+                 index_base + first, k > 0 ? 1 : 0);
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(consumed[b], compute_stream);
   }
-  if (r == CUDA_SUCCESS) r = api.cuMemcpyDtoHAsync(host_out, result, out_bytes, compute_stream);
+  for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
+    r = api.cuMemcpyDtoHAsync(host_outs[i], result_slot(i), out_bytes(ops[i]), compute_stream);
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(compute_stream);
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(copy_stream);
   for (int i = 0; i < 2; ++i) {

@@ -76,11 +76,25 @@ class Hotpath {
                        CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
                        std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream);
 
+  // Same pipeline computing the f32 sum and the argmax from one host->device
+  // transfer of each chunk (8-byte sum and 16-byte argmax record out).
+  CUresult reduce_host_sum_argmax(const void* host_in, std::uint64_t n, std::uint64_t index_base,
+                                  void* host_sum_out, void* host_argmax_out, CUdeviceptr staging,
+                                  std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
+                                  CUstream copy_stream, CUstream compute_stream);
+
   CUfunction function(const std::string& name) const;
 
  private:
   Hotpath() = default;
   CUresult launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args);
+  // Chunked, double-buffered host->device pipeline shared by the host-buffer
+  // reductions: every op in `ops` reduces each staged chunk, op i into
+  // `host_outs[i]`.
+  CUresult reduce_host_ops(const ReduceOp* ops, int nops, const void* host_in, std::uint64_t n,
+                           std::uint64_t index_base, void* const* host_outs, CUdeviceptr staging,
+                           std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
+                           CUstream copy_stream, CUstream compute_stream);
 
   CUcontext context_ = nullptr;
   CUmodule module_ = nullptr;

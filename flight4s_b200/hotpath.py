@@ -148,6 +148,20 @@ class Hotpath:
                                   stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")
         return out
 
+    def reduce_host_sum_argmax(self, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
+                               workspace: Any = None, index_base: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        """f32 sum and argmax of a host array from one transfer of each chunk;
+        returns (8-byte sum record, 16-byte argmax record)."""
+        ws = self.workspace() if workspace is None else workspace
+        s = np.zeros(1, np.uint64)
+        a = np.zeros(2, np.uint64)
+        host = np.ascontiguousarray(host)
+        check(lib.f4s_reduce_host_sum_argmax_f32(self._h, host.ctypes.data, host.size, index_base, s.ctypes.data,
+                                                 a.ctypes.data, device_address(staging), _nbytes(staging),
+                                                 device_address(ws), _nbytes(ws), stream_handle(copy_stream),
+                                                 stream_handle(compute_stream)), "reduce_host_sum_argmax")
+        return s, a
+
     # ------------------------------------------------------------ block sum
     @staticmethod
     def block_reduce_workspace_bytes(n: int) -> int:

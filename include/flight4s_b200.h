@@ -226,6 +226,15 @@ int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint6
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t workspace,
                     uint64_t workspace_bytes, uint64_t copy_stream, uint64_t compute_stream);
 
+/* The same pipeline computing the f32 sum and the argmax of one host array
+ * from a single host->device transfer of each chunk (the two reductions
+ * share every staged chunk): host_sum_out receives 8 bytes, host_argmax_out
+ * 16 bytes, as above.  Synchronizes both streams before returning. */
+int f4s_reduce_host_sum_argmax_f32(f4s_hotpath* hotpath, const void* host_in, uint64_t n, uint64_t index_base,
+                                   void* host_sum_out, void* host_argmax_out, uint64_t staging,
+                                   uint64_t staging_bytes, uint64_t workspace, uint64_t workspace_bytes,
+                                   uint64_t copy_stream, uint64_t compute_stream);
+
 /* ------------------------------------------------------------ block sum */
 
 /* The reference's blockReduceSum

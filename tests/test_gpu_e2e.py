@@ -28,3 +28,21 @@ def test_reduce_host_matches_device(ctx, hp, n):
     assert int(r[1]) == ri
     if n:
         assert int(r[0]) == orc.argmax_packed_key(rv, ri)
+
+
+@pytest.mark.parametrize("n", [0, 7, (1 << 20) + 5, 10_000_019])
+def test_reduce_host_sum_argmax_one_transfer(ctx, hp, n):
+    rng = np.random.default_rng(n + 1)
+    x = ctx.allocate_pinned("f32", n)
+    x.copy_from(rng.standard_normal(n).astype(np.float32))
+    staging = ctx.allocate("u8", 256 + 2 * (1 << 20))
+    s1, s2 = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    s, a = hp.reduce_host_sum_argmax(x.array, staging, s1, s2, index_base=1000)
+    exact, abs_sum = orc.sum_f32_exact(x.array)
+    assert abs(float(s.view(np.float64)[0]) - exact) <= 1e-5 * abs_sum
+    rv, ri = orc.argmax_f32(x.array)
+    a = a.view(np.int64)
+    if n:
+        assert int(a[1]) == ri + 1000 and int(a[0]) == orc.argmax_packed_key(rv, ri + 1000)
+    else:
+        assert int(a[1]) == -1
