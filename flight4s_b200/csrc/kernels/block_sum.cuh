@@ -68,6 +68,12 @@ __device__ __forceinline__ void tree_level(const float* src, unsigned count, flo
   }
 }
 
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned* ticket) {
+  unsigned prior;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prior) : "l"(ticket) : "memory");
+  return prior;
+}
+
 }  // namespace f4s
 
 // (in, n, partials[ceil(n/256)], out[1], workspace).  Launch with
@@ -119,15 +125,17 @@ f4s_block_reduce_sum_f32(const float* __restrict__ in, int n, float* __restrict_
     const float node = (tiles <= 1) ? w[0] : tree256(w);
     if (lane == 0) {
       level2[cluster_id] = node;
-      __threadfence();
-      is_last = (atomicAdd(ticket, 1u) == num_clusters - 1) ? 1 : 0;
+      // One acquire-release RMW orders this cluster's level-2 store before
+      // its ticket and, for the last arriver, every other cluster's store
+      // before its reads (cheaper than a full fence plus a relaxed atomic).
+      is_last = (ticket_acq_rel(ticket) == num_clusters - 1) ? 1 : 0;
     }
   }
   __syncthreads();
   if (!is_last) return;
 
-  // remaining levels on the last cluster's leader CTA
-  __threadfence();
+  // remaining levels on the last cluster's leader CTA (the barrier above
+  // carries the acquire of thread 0 to the CTA's other threads)
   unsigned count = num_clusters;
   if (count == 1) {
     if (threadIdx.x == 0) {

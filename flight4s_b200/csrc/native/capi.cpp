@@ -370,6 +370,17 @@ int f4s_hotpath_set_reduce_cluster(f4s_hotpath* hotpath, int32_t cluster) {
   return guarded([&] { return op_status(hot(hotpath).set_reduce_cluster(cluster)); });
 }
 
+int f4s_hotpath_wait_timeouts(f4s_hotpath* hotpath, uint32_t* count, int32_t reset) {
+  return guarded([&] {
+    require_out(count, "timeout count");
+    return op_status(hot(hotpath).wait_timeouts(count, reset != 0));
+  });
+}
+
+int f4s_hotpath_check_bounded_wait(f4s_hotpath* hotpath, uint32_t polls) {
+  return guarded([&] { return op_status(hot(hotpath).check_bounded_wait(polls)); });
+}
+
 uint64_t f4s_reduce_workspace_bytes(const f4s_hotpath* hotpath) {
   return (hotpath && hotpath->impl) ? hotpath->impl->reduce_workspace_bytes() : 0;
 }

@@ -104,6 +104,31 @@ Hotpath::~Hotpath() {
   }
 }
 
+CUresult Hotpath::wait_timeouts(std::uint32_t* count, bool reset) {
+  const DriverApi& api = require_driver();
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  CUdeviceptr addr = 0;
+  std::size_t bytes = 0;
+  CUresult r = api.cuModuleGetGlobal(&addr, &bytes, module_, "f4s_wait_timeouts");
+  if (r == CUDA_SUCCESS && bytes != sizeof(std::uint32_t)) r = CUDA_ERROR_INVALID_VALUE;
+  if (r == CUDA_SUCCESS) r = api.cuCtxSynchronize();
+  if (r == CUDA_SUCCESS) r = api.cuMemcpyDtoH(count, addr, sizeof(std::uint32_t));
+  if (r == CUDA_SUCCESS && reset) {
+    const std::uint32_t zero = 0;
+    r = api.cuMemcpyHtoD(addr, &zero, sizeof(zero));
+  }
+  return cur.finish(r);
+}
+
+CUresult Hotpath::check_bounded_wait(std::uint32_t polls) {
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.u32(polls);
+  return cur.finish(launch(function("f4s_check_bounded_wait"), nullptr, 1, 32, 0, args));
+}
+
 CUfunction Hotpath::function(const std::string& name) const {
   const DriverApi& api = require_driver();
   CUfunction fn = nullptr;
@@ -298,6 +323,16 @@ CUresult Hotpath::rmsnorm_rows(CUstream stream, CUdeviceptr in, CUdeviceptr weig
   if (!(eps >= 0.0f)) throw std::invalid_argument("eps must be a non-negative number");
   int vpt = row_vectors_per_thread(cols, in, out);
   if (weight % 16 != 0) vpt = 0;
+  if (vpt == 4) {
+    // 2049..8192-wide rows: TMA-staged kernel, 2 persistent CTAs per SM
+    // (the measured optimum; rows are 16-byte aligned because cols % 8 == 0).
+    Current cur(context_);
+    if (cur.result() != CUDA_SUCCESS) return cur.result();
+    ArgumentPack args;
+    args.ptr(in).ptr(weight).ptr(out).i32(rows).i32(cols).f32(eps);
+    const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * 2));
+    return cur.finish(launch(function("f4s_rmsnorm_rows_bf16_tma"), stream, grid, kRowBlock, 0, args));
+  }
   const std::string name = vpt ? "f4s_rmsnorm_rows_bf16_v" + std::to_string(vpt) : "f4s_rmsnorm_rows_bf16_any";
   const CUfunction fn = function(name);
   int per_sm = shape_.row_ctas_per_sm;

@@ -83,6 +83,13 @@ class Hotpath {
                                   std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
                                   CUstream copy_stream, CUstream compute_stream);
 
+  // Bounded device-side waits that gave up since the last reset (read after
+  // synchronizing the context); non-zero means some output was not written.
+  CUresult wait_timeouts(std::uint32_t* count, bool reset);
+  // Launches a one-thread kernel whose wait can never be satisfied, bounded
+  // to `polls` polls: exercises the give-up path on the device.
+  CUresult check_bounded_wait(std::uint32_t polls);
+
   CUfunction function(const std::string& name) const;
 
  private:

@@ -87,6 +87,17 @@ class Hotpath:
             self._result = self.context.allocate("u64", 2)
         return self._result
 
+    def wait_timeouts(self, reset: bool = False) -> int:
+        """Bounded device waits that gave up since the last reset (0 when
+        every staged row arrived); synchronizes the context."""
+        n = C.c_uint32()
+        check(lib.f4s_hotpath_wait_timeouts(self._h, C.byref(n), int(reset)), "wait-timeout count")
+        return int(n.value)
+
+    def check_bounded_wait(self, polls: int) -> None:
+        """Run the diagnostic kernel whose wait cannot complete (bounded)."""
+        check(lib.f4s_hotpath_check_bounded_wait(self._h, polls), "bounded-wait check")
+
     def set_reduce_cluster(self, cluster: int) -> None:
         check(lib.f4s_hotpath_set_reduce_cluster(self._h, cluster), "reduction cluster size")
 

@@ -189,6 +189,16 @@ int f4s_hotpath_sm_count(const f4s_hotpath* hotpath);
 /* CTAs per cluster of the full-array reductions (1..8, default 4). */
 int f4s_hotpath_set_reduce_cluster(f4s_hotpath* hotpath, int32_t cluster);
 
+/* Device-side waits never spin forever: a kernel that waits on a barrier
+ * (the TMA-staged RMSNorm) gives up after a bounded number of polls,
+ * leaves its remaining rows unwritten and counts the event.  This reads the
+ * count (after synchronizing the context) and optionally clears it. */
+int f4s_hotpath_wait_timeouts(f4s_hotpath* hotpath, uint32_t* count, int32_t reset);
+/* Diagnostic: launches one thread that waits, bounded to `polls` polls, on
+ * a barrier nothing will complete, so the give-up path runs on the device
+ * and raises the count above.  Asynchronous on the legacy default stream. */
+int f4s_hotpath_check_bounded_wait(f4s_hotpath* hotpath, uint32_t polls);
+
 /* ---------------------------------------------- full-array reductions */
 
 /* Workspace (device bytes) every reduction on this hotpath needs: a ticket

@@ -68,7 +68,8 @@ def test_invalid_ptx_reports_jit_error_log(ctx):
 def test_hotpath_kernels_resolve_with_attributes(ctx, hp):
     for name in ["f4s_reduce_sum_f32", "f4s_reduce_sum_i32", "f4s_reduce_argmax_f32", "f4s_block_reduce_sum_f32",
                  "f4s_vector_add_f32", "f4s_vector_add_bf16", "f4s_softmax_rows_bf16_v4", "f4s_rmsnorm_rows_bf16_v4",
-                 "f4s_fp8_quant_flat", "f4s_fp8_dequant_flat", "f4s_fill_synthetic"]:
+                 "f4s_fp8_quant_flat", "f4s_fp8_dequant_flat", "f4s_fill_synthetic",
+                 "f4s_rmsnorm_rows_bf16_tma", "f4s_check_bounded_wait"]:
         fn = hp.module.function(name)
         assert fn.attributes.registers_per_thread > 0 and fn.attributes.local_memory_bytes == 0, name
 

@@ -98,3 +98,23 @@ def test_full_size_32768x8192_against_torch_fp32(ctx, hp, torch_dev):
     assert err <= ATOL_RMS
     del x, y, ref, xf
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 8192), (3, 2056 * 2), (300, 4104), (1000, 8192), (5000, 6144)])
+def test_rmsnorm_tma_staged_matches_register_kernel_bitwise(ctx, hp, rows, cols):
+    """Rows of 2049..8192 go through the TMA-staged kernel; it must equal the
+    register-resident kernel bit for bit, and no staged wait may give up."""
+    rng = np.random.default_rng(rows + cols)
+    x = orc.f32_to_bf16(rng.standard_normal(rows * cols).astype(np.float32))
+    w = orc.f32_to_bf16((1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32))
+    dx, dw, dy, dr = _bf16(ctx, x), _bf16(ctx, w), ctx.allocate("bf16", x.size), ctx.allocate("bf16", x.size)
+    hp.wait_timeouts(reset=True)
+    hp.rmsnorm_rows_bf16(dx, dw, dy, rows, cols, eps=1e-6)
+    fn = hp.module.function("f4s_rmsnorm_rows_bf16_v4",
+                            signature=[f4s.DEVPTR, f4s.DEVPTR, f4s.DEVPTR, f4s.INT32, f4s.INT32, f4s.FLOAT32])
+    fn.launch(fn.bind(dx, dw, dr, rows, cols, 1e-6), f4s.LaunchConfig(f4s.Grid(min(rows, 296)), f4s.Block(256)))
+    ctx.synchronize()
+    assert hp.wait_timeouts() == 0
+    assert np.array_equal(dy.copy_to_array(), dr.copy_to_array())
+    y = orc.bf16_to_f32(dy.copy_to_array()).reshape(rows, cols)
+    assert np.allclose(y, orc.rmsnorm_rows(x, w, rows, cols, 1e-6), rtol=RTOL, atol=ATOL_RMS)
