@@ -2,6 +2,7 @@
 
 #include <dlfcn.h>
 
+#include <cstdlib>
 #include <mutex>
 
 namespace flight4s::cuda {
@@ -18,15 +19,19 @@ struct Loaded {
 
 Loaded load() {
   Loaded l;
-  void* lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+  // FLIGHT4S_CUDA_DRIVER names another driver library (the tests point it
+  // at a fake that records launches and injects errors).
+  const char* override_path = std::getenv("FLIGHT4S_CUDA_DRIVER");
+  const std::string name = (override_path && *override_path) ? override_path : "libcuda.so.1";
+  void* lib = dlopen(name.c_str(), RTLD_NOW | RTLD_GLOBAL);
   if (lib == nullptr) {
     const char* err = dlerror();
-    l.why = std::string("cannot load libcuda.so.1: ") + (err ? err : "unknown dlopen error");
+    l.why = "cannot load " + name + ": " + (err ? err : "unknown dlopen error");
     return l;
   }
   auto get = reinterpret_cast<GetProcAddress>(dlsym(lib, "cuGetProcAddress_v2"));
   if (get == nullptr) {
-    l.why = "libcuda.so.1 does not export cuGetProcAddress_v2 (driver older than CUDA 12)";
+    l.why = name + " does not export cuGetProcAddress_v2 (driver older than CUDA 12)";
     return l;
   }
 #define F4S_DRIVER_FN(name)                                                                \

@@ -2,7 +2,8 @@
 //
 // The library resolves libcuda at first use (dlopen + cuGetProcAddress)
 // instead of linking it, so it loads, and reports a clean error, on hosts
-// that have no NVIDIA driver.  Function-pointer types come from <cuda.h>, so
+// that have no NVIDIA driver.  FLIGHT4S_CUDA_DRIVER, when set, names the
+// driver library to open instead of libcuda.so.1.  Function-pointer types come from <cuda.h>, so
 // every entry has the exact versioned prototype the driver hands back.
 #pragma once
 

@@ -1,0 +1,186 @@
+"""Scenarios run against the fake CUDA driver (tests/fake_driver/fake_cuda.c),
+one per process: `python _fake_driver_scenarios.py <scenario> <libfakecuda.so>`
+with FLIGHT4S_CUDA_DRIVER pointing at the fake (set by
+tests/test_fake_driver.py).  Exit status 0 = pass."""
+import ctypes as C
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import flight4s_b200 as f4s
+from flight4s_b200 import _native
+
+FAKE = C.CDLL(sys.argv[2])
+
+
+class Launch(C.Structure):
+    _fields_ = [("name", C.c_char * 64), ("grid", C.c_uint * 3), ("block", C.c_uint * 3), ("smem", C.c_uint),
+                ("cluster", C.c_int), ("cluster_dim", C.c_uint * 3), ("nparams", C.c_int),
+                ("params", (C.c_ubyte * 8) * 32), ("stream", C.c_ulonglong)]
+
+
+FAKE.fake_last_launch.restype = C.POINTER(Launch)
+
+
+def last() -> Launch:
+    return FAKE.fake_last_launch().contents
+
+
+def count() -> int:
+    return FAKE.fake_launch_count()
+
+
+def param(launch: Launch, i: int, size: int = 8) -> int:
+    return int.from_bytes(bytes(launch.params[i])[:size], "little")
+
+
+def expect_failure(fn, code: int, name: str):
+    try:
+        fn()
+    except f4s.CudaDriverFailure as e:
+        assert e.result_code == code and e.result_name == name, (e.result_code, e.result_name)
+        return e
+    raise AssertionError("expected a driver failure")
+
+
+def launch_records_geometry():
+    ctx = f4s.CudaContext.open(0)
+    assert ctx.compute_capability == (10, 0)
+    mod = ctx.load(b"fake module image")
+    fn = mod.function("write_values", signature=[f4s.DEVPTR, f4s.INT32])
+    buf = ctx.allocate("i32", 64)
+    fn.launch(fn.bind(buf, 100), f4s.LaunchConfig(f4s.Grid(2), f4s.Block(32), cluster=f4s.Cluster(2)))
+    L = last()
+    assert L.name == b"write_values" and tuple(L.grid) == (2, 1, 1) and tuple(L.block) == (32, 1, 1)
+    assert L.cluster == 1 and tuple(L.cluster_dim) == (2, 1, 1)
+    assert param(L, 0) == buf.address and param(L, 1, 4) == 100
+    fn.launch(fn.bind(buf, 7), f4s.LaunchConfig(f4s.Grid(4, 2), f4s.Block(16, 2), dynamic_shared_memory_bytes=256))
+    L = last()
+    assert L.cluster == 0 and tuple(L.grid) == (4, 2, 1) and tuple(L.block) == (16, 2, 1) and L.smem == 256
+    assert count() == 2
+    ctx.close()
+
+
+def launch_error_propagates():
+    ctx = f4s.CudaContext.open(0)
+    fn = ctx.load(b"fake").function("write_values", signature=[f4s.DEVPTR, f4s.INT32])
+    buf = ctx.allocate("i32", 64)
+    e = expect_failure(lambda: fn.launch(fn.bind(buf, 1), f4s.LaunchConfig(f4s.Grid(1), f4s.Block(32))), 719,
+                       "CUDA_ERROR_LAUNCH_FAILED")
+    assert e.description == "fake driver error description"
+    assert count() == 0
+    hp = ctx.hotpath()
+    expect_failure(lambda: hp.vector_add_f32(buf, buf, buf, n=64), 719, "CUDA_ERROR_LAUNCH_FAILED")
+
+
+def out_of_memory():
+    ctx = f4s.CudaContext.open(0)
+    expect_failure(lambda: ctx.allocate("f32", 1 << 20), 2, "CUDA_ERROR_OUT_OF_MEMORY")
+    # a hotpath cannot get its workspace either, and says so
+    hp = ctx.hotpath()
+    expect_failure(lambda: hp.workspace(), 2, "CUDA_ERROR_OUT_OF_MEMORY")
+
+
+def pop_mismatch():
+    """The operation succeeds but another context is on top afterwards:
+    reported as CUDA_ERROR_INVALID_CONTEXT (native/src/current_context_scope.cpp:21-33)."""
+    ctx = f4s.CudaContext.open(0)
+    expect_failure(ctx.synchronize, 201, "CUDA_ERROR_INVALID_CONTEXT")
+    expect_failure(lambda: ctx.allocate("f32", 16), 201, "CUDA_ERROR_INVALID_CONTEXT")
+
+
+def push_failure():
+    ctx = f4s.CudaContext.open(0)
+    rc = _native.lib.f4s_launch_kernel(ctx.handle, 0x1000, 0, 1, 1, 1, 32, 1, 1, 0, 0, 0, 0, 0, None, 0, None, None, 0)
+    assert rc == 201 and _native.last_status()[1] == "CUDA_ERROR_INVALID_CONTEXT"
+    assert count() == 0
+
+
+def jit_error_log():
+    ctx = f4s.CudaContext.open(0)
+    e = expect_failure(lambda: ctx.load_ptx(b".version 8.7\n"), 218, "CUDA_ERROR_INVALID_PTX")
+    assert e.error_log == "fake error log"
+
+
+def invalid_arguments_never_reach_driver():
+    ctx = f4s.CudaContext.open(0)
+    fn = ctx.load(b"fake").function("write_values", signature=[f4s.DEVPTR, f4s.INT32])
+    buf = ctx.allocate("i32", 64)
+    st = fn.bind(buf, 1).storage()
+    rc = _native.lib.f4s_launch_kernel(ctx.handle, fn.handle, 0, 3, 1, 1, 32, 1, 1, 0, 1, 2, 1, 1, st.address,
+                                       st.size_bytes, st.offsets, st.codes, st.count)
+    assert rc == _native.STATUS_INVALID_ARGUMENT and "must be divisible" in _native.last_status()[2]
+    hp = ctx.hotpath()
+    for bad in [lambda: hp.vector_add_f32(buf.address + 1, buf, buf, n=8),
+                lambda: hp.softmax_rows_bf16(buf, buf, -1, 8),
+                lambda: hp.reduce_into(f4s.REDUCE_SUM_F32, buf, buf.address + 4, workspace=buf),
+                lambda: hp.fill_synthetic(buf, 8, f4s.UNIFORM_I32, seed=1, ilo=3, ihi=2)]:
+        try:
+            bad()
+        except ValueError:
+            pass
+        else:
+            raise AssertionError("expected ValueError")
+    assert count() == 0
+
+
+def hotpath_dispatch():
+    ctx = f4s.CudaContext.open(0)
+    hp = ctx.hotpath()
+    assert hp.sm_count == 148
+    big = ctx.allocate("f32", 1 << 28)
+
+    def check(name, grid, block=256, cluster=None):
+        L = last()
+        assert L.name.decode() == name, (L.name, name)
+        assert tuple(L.grid) == (grid, 1, 1) and L.block[0] == block, (name, tuple(L.grid), L.block[0])
+        if cluster is None:
+            assert L.cluster == 0
+        else:
+            assert L.cluster == 1 and L.cluster_dim[0] == cluster
+        return L
+
+    hp.vector_add_f32(big, big, big, n=1 << 28)
+    assert param(check("f4s_vector_add_f32", (1 << 28) // 2048), 3, 4) == 1 << 28
+    hp.vector_add_bf16(big, big, big, n=1000)
+    check("f4s_vector_add_bf16", 1)
+    hp.softmax_rows_bf16(big, big, 32768, 8192)
+    check("f4s_softmax_rows_bf16_v4", 32768)
+    hp.softmax_rows_bf16(big, big, 10, 1000)
+    check("f4s_softmax_rows_bf16_v1", 10)
+    hp.softmax_rows_bf16(big, big, 10, 1001)
+    check("f4s_softmax_rows_bf16_any", 10)
+    hp.rmsnorm_rows_bf16(big, big, big, 32768, 8192)
+    check("f4s_rmsnorm_rows_bf16_tma", 296)
+    hp.rmsnorm_rows_bf16(big, big, big, 32768, 16384)
+    check("f4s_rmsnorm_rows_bf16_v8", 148 * 8)
+    hp.rmsnorm_rows_bf16(big, big, big, 5, 1001)
+    check("f4s_rmsnorm_rows_bf16_any", 5)
+    hp.fp8_quantize_e4m3(big, big, big, 16384, 16384)
+    assert param(check("f4s_fp8_quant_flat", (1 << 21) // 16 // 8), 3, 4) == 1 << 21
+    hp.fp8_dequantize_e4m3(big, big, big, 16384, 16384)
+    check("f4s_fp8_dequant_flat", (1 << 21) // 8 // 8)
+    hp.fp8_quantize_e4m3(big, big, big, 3, 200)
+    check("f4s_fp8_quant_rows", hp_fp8_rows_grid())
+    out = ctx.allocate("i64", 2)
+    hp.reduce_into(f4s.REDUCE_SUM_F32, big, out, n=1 << 32)
+    L = check("f4s_reduce_sum_f32", 37 * 8 * 4, block=512, cluster=4)
+    assert (param(L, 1, 4), param(L, 2, 4)) == (0, 1)  # n = 2^32 split in two u32
+    hp.reduce_into(f4s.REDUCE_ARGMAX_F32, big, out, n=1000, index_base=(1 << 32) + 5, accumulate=True)
+    L = check("f4s_reduce_argmax_f32", 4, block=512, cluster=4)
+    assert (param(L, 5, 4), param(L, 6, 4), param(L, 7, 4)) == (5, 1, 1)
+    parts = ctx.allocate("f32", 4096)
+    ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
+    hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)
+    check("f4s_block_reduce_sum_f32", 128, block=1024, cluster=8)
+    ctx.close()
+
+
+def hp_fp8_rows_grid():
+    return 148 * 4  # SM count x fake occupancy
+
+
+if __name__ == "__main__":
+    globals()[sys.argv[1]]()
+    print("ok", sys.argv[1])
