@@ -433,6 +433,13 @@ def profile_run(which: str) -> None:
             hp.fill_synthetic(x, n, f4s.UNIFORM_I32, seed=SEED, ilo=-1000, ihi=1000)
             rep(lambda: hp.reduce_into(f4s.REDUCE_SUM_I32, x, out))
         del x
+    typed = [k for k in ("bf16", "f16", "e4m3", "e5m2", "f64", "u32") if want(f"reduce_sum_{k}")]
+    if typed:
+        raw = torch.randint(0, 256, (1 << 30,), dtype=torch.uint8, device=dev)
+        out = torch.zeros(2, dtype=torch.int64, device=dev)
+        for k in typed:
+            rep(lambda: hp.reduce_sum_into(k, raw, out, n=(1 << 30) // f4s.hotpath.SUM_TYPE_BYTES[k]))
+        del raw
     if want("vector_add_f32") or want("vector_add_bf16"):
         m = 1 << 26
         for dtype, kind, fn, key in [(torch.float32, f4s.UNIFORM_F32, hp.vector_add_f32, "vector_add_f32"),
@@ -565,6 +572,16 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     flushed = graph_ms(lambda: (flush.zero_(), bs()), 50) - graph_ms(lambda: flush.zero_(), 50)
     row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, flushed, timing="cuda graph")
     del flush
+
+    # ReduceSum over the other accumulator input types, 8 GiB of input each
+    # (random bits; larger than L2, so no flush is needed between launches)
+    raw = torch.randint(0, 256, (8 << 30,), dtype=torch.uint8, device=dev)
+    acc = torch.zeros(2, dtype=torch.int64, device=dev)
+    for dtype, size in [("bf16", 2), ("f16", 2), ("e4m3", 1), ("e5m2", 1), ("f64", 8), ("u32", 4)]:
+        count = (8 << 30) // size
+        row(f"reduce_sum_{dtype} 8 GiB", 8 << 30, count,
+            timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream), reps=10))
+    del raw
 
     rows, cols = 32768, 8192
     xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)

@@ -109,6 +109,28 @@ __device__ __forceinline__ float2 unpack_e4m3x2(uint32_t codes) {
   return make_float2(lo, hi);
 }
 
+// Packed e5m2x2 (low 16 bits) -> two f32, exact (E5M2 is a subset of f16).
+__device__ __forceinline__ float2 unpack_e5m2x2(uint32_t codes) {
+  uint32_t h2;
+  uint16_t c = static_cast<uint16_t>(codes);
+  asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(c));
+  float lo, hi;
+  asm("{.reg .f16 l, h;\n"
+      " mov.b32 {l, h}, %2;\n"
+      " cvt.f32.f16 %0, l;\n"
+      " cvt.f32.f16 %1, h;}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(h2));
+  return make_float2(lo, hi);
+}
+
+// IEEE binary16 bits -> f32, exact.
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  float f;
+  asm("{.reg .f16 t;\n mov.b16 t, %1;\n cvt.f32.f16 %0, t;}" : "=f"(f) : "h"(h));
+  return f;
+}
+
 // ---------------------------------------------------------------- total order
 // Signed-int image of an f32 under IEEE-754 totalOrder:
 // -NaN < -inf < ... < -0 < +0 < ... < +inf < +NaN.

@@ -57,28 +57,40 @@ __device__ __forceinline__ void argmax_merge(ArgmaxPartial& a, const ArgmaxParti
 // scalar head/tail step, the partial type with its identity / merge / warp
 // merge, and how the final partial is written to `out`.
 
-struct SumF32Op {
+__device__ __forceinline__ float u2f(uint32_t b) { return __uint_as_float(b); }
+
+// Pairwise tree over the kReduceUnroll per-vector fp32 sums, then one f64
+// add: the accumulation rule of every floating-point sum below.
+__device__ __forceinline__ double fold_unrolled(float (&s)[kReduceUnroll]) {
+#pragma unroll
+  for (int w = 1; w < kReduceUnroll; w <<= 1) {
+#pragma unroll
+    for (int u = 0; u + w < kReduceUnroll; u += 2 * w) s[u] += s[u + w];
+  }
+  return static_cast<double>(s[0]);
+}
+
+// The same tree in f64 over the per-vector f32 sums of the narrow types:
+// an E4M3 vector sum is exact in f32, so E4M3 totals stay exact while they
+// fit f64's 53 bits at the 2^-9 grid (below 2^44, i.e. any n < 2^35).
+__device__ __forceinline__ double fold_unrolled_f64(const float (&s)[kReduceUnroll]) {
+  double d[kReduceUnroll];
+#pragma unroll
+  for (int u = 0; u < kReduceUnroll; ++u) d[u] = static_cast<double>(s[u]);
+#pragma unroll
+  for (int w = 1; w < kReduceUnroll; w <<= 1) {
+#pragma unroll
+    for (int u = 0; u + w < kReduceUnroll; u += 2 * w) d[u] += d[u + w];
+  }
+  return d[0];
+}
+
+struct SumF64PartialBase {
   using Partial = double;
   struct Thread {
     double acc = 0.0;
   };
-  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t, uint64_t, int count) {
-    float s[kReduceUnroll];
-#pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) {
-      s[u] = (u < count) ? (v[u].x + v[u].y) + (v[u].z + v[u].w) : 0.0f;
-    }
-#pragma unroll
-    for (int w = 1; w < kReduceUnroll; w <<= 1) {
-#pragma unroll
-      for (int u = 0; u + w < kReduceUnroll; u += 2 * w) s[u] += s[u + w];
-    }
-    t.acc += static_cast<double>(s[0]);
-  }
-  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t) {
-    t.acc += static_cast<double>(x);
-  }
-  static __device__ __forceinline__ Partial finish(Thread& t, const float*, uint64_t) { return t.acc; }
+  static __device__ __forceinline__ Partial finish(Thread& t, uint64_t) { return t.acc; }
   static __device__ __forceinline__ Partial identity() { return 0.0; }
   static __device__ __forceinline__ Partial merge(Partial a, Partial b) { return a + b; }
   static __device__ __forceinline__ Partial warp_merge(Partial v) { return warp_sum_f64(v); }
@@ -89,26 +101,113 @@ struct SumF32Op {
   }
 };
 
-struct SumI32Op {
+// f32 in, f64 out: fp32 pairs inside a 16-byte vector, f64 above.
+struct SumF32Op : SumF64PartialBase {
+  static constexpr int kElemBytes = 4;
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
+    float s[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      s[u] = (u < count) ? (u2f(v[u].x) + u2f(v[u].y)) + (u2f(v[u].z) + u2f(v[u].w)) : 0.0f;
+    }
+    t.acc += fold_unrolled(s);
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
+    t.acc += static_cast<double>(u2f(static_cast<uint32_t>(bits)));
+  }
+};
+
+// 16-bit floats (bf16 or f16) in, f64 out: the eight elements of a vector
+// are widened exactly to f32 and summed pairwise in f32.
+template <bool kBf16>
+struct SumHalfOp : SumF64PartialBase {
+  static constexpr int kElemBytes = 2;
+  static __device__ __forceinline__ float lo(uint32_t w) {
+    if constexpr (kBf16) return bf16_lo(w); else return f16_to_f32(static_cast<uint16_t>(w));
+  }
+  static __device__ __forceinline__ float hi(uint32_t w) {
+    if constexpr (kBf16) return bf16_hi(w); else return f16_to_f32(static_cast<uint16_t>(w >> 16));
+  }
+  static __device__ __forceinline__ float pair(uint32_t w) { return lo(w) + hi(w); }
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
+    float s[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      s[u] = (u < count) ? (pair(v[u].x) + pair(v[u].y)) + (pair(v[u].z) + pair(v[u].w)) : 0.0f;
+    }
+    t.acc += fold_unrolled_f64(s);
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
+    const uint32_t w = static_cast<uint32_t>(bits);
+    t.acc += static_cast<double>(lo(w));
+  }
+};
+
+// FP8 (E4M3 or E5M2) in, f64 out: sixteen codes per vector, decoded exactly
+// through f16 and summed pairwise in f32 (exact for E4M3); vector sums are
+// combined in f64.
+template <bool kE4m3>
+struct SumFp8Op : SumF64PartialBase {
+  static constexpr int kElemBytes = 1;
+  static __device__ __forceinline__ float2 dec2(uint32_t two_codes) {
+    if constexpr (kE4m3) return unpack_e4m3x2(two_codes); else return unpack_e5m2x2(two_codes);
+  }
+  static __device__ __forceinline__ float quad(uint32_t w) {
+    const float2 a = dec2(w & 0xFFFFu), b = dec2(w >> 16);
+    return (a.x + a.y) + (b.x + b.y);
+  }
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
+    float s[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      s[u] = (u < count) ? (quad(v[u].x) + quad(v[u].y)) + (quad(v[u].z) + quad(v[u].w)) : 0.0f;
+    }
+    t.acc += fold_unrolled_f64(s);
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
+    t.acc += static_cast<double>(dec2(static_cast<uint32_t>(bits) & 0xFFu).x);
+  }
+};
+
+// f64 in, f64 out.
+struct SumF64Op : SumF64PartialBase {
+  static constexpr int kElemBytes = 8;
+  static __device__ __forceinline__ double d(uint32_t lo, uint32_t hi) {
+    return __hiloint2double(static_cast<int>(hi), static_cast<int>(lo));
+  }
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
+    double s[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) s[u] = (u < count) ? d(v[u].x, v[u].y) + d(v[u].z, v[u].w) : 0.0;
+#pragma unroll
+    for (int w = 1; w < kReduceUnroll; w <<= 1) {
+#pragma unroll
+      for (int u = 0; u + w < kReduceUnroll; u += 2 * w) s[u] += s[u + w];
+    }
+    t.acc += s[0];
+  }
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
+    t.acc += __longlong_as_double(static_cast<long long>(bits));
+  }
+};
+
+// i32 or u32 in, 32-bit two's-complement wrap out (bit-identical for both).
+struct SumWrap32Op {
+  static constexpr int kElemBytes = 4;
   using Partial = int32_t;
   struct Thread {
     uint32_t acc = 0;
   };
-  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t, uint64_t, int count) {
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
-      if (u < count) {
-        t.acc += (__float_as_uint(v[u].x) + __float_as_uint(v[u].y)) +
-                 (__float_as_uint(v[u].z) + __float_as_uint(v[u].w));
-      }
+      if (u < count) t.acc += (v[u].x + v[u].y) + (v[u].z + v[u].w);
     }
   }
-  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t) {
-    t.acc += __float_as_uint(x);
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
+    t.acc += static_cast<uint32_t>(bits);
   }
-  static __device__ __forceinline__ Partial finish(Thread& t, const float*, uint64_t) {
-    return static_cast<int32_t>(t.acc);
-  }
+  static __device__ __forceinline__ Partial finish(Thread& t, uint64_t) { return static_cast<int32_t>(t.acc); }
   static __device__ __forceinline__ Partial identity() { return 0; }
   static __device__ __forceinline__ Partial merge(Partial a, Partial b) {
     return static_cast<int32_t>(static_cast<uint32_t>(a) + static_cast<uint32_t>(b));
@@ -130,14 +229,16 @@ struct SumI32Op {
 //            while index < 2^32; INT64_MIN for an empty input;
 //   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
 struct ArgmaxF32Op {
+  static constexpr int kElemBytes = 4;
   using Partial = ArgmaxPartial;
   struct Thread {
     int32_t vkey = INT32_MIN;  // best key seen in the vector body
     uint64_t best_vec = UINT64_MAX;
-    float4 best = make_float4(0.f, 0.f, 0.f, 0.f);  // that vector's values
+    uint4 best = make_uint4(0, 0, 0, 0);  // that vector's values
     ArgmaxPartial s{INT32_MIN, INT64_MAX};  // scalar head/tail candidate
   };
-  static __device__ __forceinline__ void body(Thread& t, const float4* v, uint64_t base,
+  static __device__ __forceinline__ int32_t key(uint32_t b) { return total_order_key(__uint_as_float(b)); }
+  static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t base,
                                               uint64_t stride, int count) {
     // The hot loop tracks only the best vector (kept in registers; the
     // update branch is rarely taken); the lane inside it is resolved once
@@ -146,9 +247,7 @@ struct ArgmaxF32Op {
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
       if (u < count) {
-        const int32_t k =
-            max(max(total_order_key(v[u].x), total_order_key(v[u].y)),
-                max(total_order_key(v[u].z), total_order_key(v[u].w)));
+        const int32_t k = max(max(key(v[u].x), key(v[u].y)), max(key(v[u].z), key(v[u].w)));
         if (k > t.vkey) {
           t.vkey = k;
           t.best_vec = base + u * stride;
@@ -157,17 +256,17 @@ struct ArgmaxF32Op {
       }
     }
   }
-  static __device__ __forceinline__ void scalar(Thread& t, float x, uint64_t index) {
-    argmax_merge(t.s, ArgmaxPartial{total_order_key(x), static_cast<int64_t>(index)});
+  static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t index) {
+    argmax_merge(t.s, ArgmaxPartial{key(static_cast<uint32_t>(bits)), static_cast<int64_t>(index)});
   }
-  static __device__ __forceinline__ Partial finish(Thread& t, const float* in, uint64_t head) {
+  static __device__ __forceinline__ Partial finish(Thread& t, uint64_t head) {
     ArgmaxPartial p = t.s;
     if (t.best_vec != UINT64_MAX) {
-      const float4 v = t.best;
+      const uint4 v = t.best;
       int lane = 3;
-      if (total_order_key(v.z) == t.vkey) lane = 2;
-      if (total_order_key(v.y) == t.vkey) lane = 1;
-      if (total_order_key(v.x) == t.vkey) lane = 0;
+      if (key(v.z) == t.vkey) lane = 2;
+      if (key(v.y) == t.vkey) lane = 1;
+      if (key(v.x) == t.vkey) lane = 0;
       argmax_merge(p, ArgmaxPartial{t.vkey, static_cast<int64_t>(head + 4 * t.best_vec + lane)});
     }
     return p;
@@ -219,12 +318,24 @@ __device__ __forceinline__ void store_partial<ArgmaxPartial>(unsigned char* slot
 }
 
 // --------------------------------------------------------------- the kernel
+template <int kBytes>
+__device__ __forceinline__ uint64_t load_element_bits(const unsigned char* p) {
+  if constexpr (kBytes == 1) return *p;
+  else if constexpr (kBytes == 2) return *reinterpret_cast<const uint16_t*>(p);
+  else if constexpr (kBytes == 4) return *reinterpret_cast<const uint32_t*>(p);
+  else return *reinterpret_cast<const unsigned long long*>(p);
+}
+
+// in: n elements of Op::kElemBytes bytes, aligned to the element size.
 template <class Op>
-__device__ __forceinline__ void reduce_full(const float* __restrict__ in, uint64_t n,
+__device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uint64_t n,
                                             void* __restrict__ out,
                                             unsigned char* __restrict__ workspace,
                                             uint64_t index_base, int accumulate) {
   using Partial = typename Op::Partial;
+  constexpr int kElem = Op::kElemBytes;
+  constexpr int kPerVec = 16 / kElem;
+  const unsigned char* in = static_cast<const unsigned char*>(in_ptr);
   const cg::cluster_group cluster = cg::this_cluster();
 
   __shared__ Partial warp_partials[kReduceBlock / kWarp];
@@ -235,43 +346,38 @@ __device__ __forceinline__ void reduce_full(const float* __restrict__ in, uint64
   const uint64_t nthreads = static_cast<uint64_t>(gridDim.x) * blockDim.x;
 
   // [0,n) = scalar head up to the first 16-byte boundary, vector body,
-  // scalar tail (< 4 elements each).
+  // scalar tail (fewer than one vector each).
   const uint64_t addr = reinterpret_cast<uint64_t>(in);
-  uint64_t head = ((16u - (addr & 15u)) & 15u) / 4u;
+  uint64_t head = ((16u - (addr & 15u)) & 15u) / kElem;
   if (head > n) head = n;
-  const uint64_t nvec = (n - head) / 4u;
-  const uint64_t tail_begin = head + 4u * nvec;
+  const uint64_t nvec = (n - head) / kPerVec;
+  const uint64_t tail_begin = head + static_cast<uint64_t>(kPerVec) * nvec;
 
   typename Op::Thread t;
-  if (tid < head) Op::scalar(t, in[tid], tid);
-  if (tid < n - tail_begin) Op::scalar(t, in[tail_begin + tid], tail_begin + tid);
+  for (uint64_t i = tid; i < head; i += nthreads) Op::scalar(t, load_element_bits<kElem>(in + i * kElem), i);
+  for (uint64_t i = tail_begin + tid; i < n; i += nthreads)
+    Op::scalar(t, load_element_bits<kElem>(in + i * kElem), i);
 
-  const float4* vin = reinterpret_cast<const float4*>(in + head);
+  const uint4* vin = reinterpret_cast<const uint4*>(in + head * kElem);
   const uint64_t step = nthreads * kReduceUnroll;
   uint64_t base = tid;
   for (; base + (kReduceUnroll - 1) * nthreads < nvec; base += step) {
-    float4 v[kReduceUnroll];
+    uint4 v[kReduceUnroll];
 #pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_f4(vin + base + u * nthreads);
+    for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_u4(vin + base + u * nthreads);
     Op::body(t, v, base, nthreads, kReduceUnroll);
   }
-  if (base < nvec) {
-    float4 v[kReduceUnroll];
-    int count = 0;
-#pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) {
-      if (base + u * nthreads < nvec) {
-        v[u] = ld_stream_f4(vin + base + u * nthreads);
-        count = u + 1;
-      } else {
-        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    Op::body(t, v, base, nthreads, count);
+  // Fewer than kReduceUnroll vectors left for this thread: one at a time
+  // (a rolled loop keeps the unrolled body's registers free).
+#pragma unroll 1
+  for (; base < nvec; base += nthreads) {
+    uint4 v[kReduceUnroll];
+    v[0] = ld_stream_u4(vin + base);
+    Op::body(t, v, base, nthreads, 1);
   }
 
   // thread -> warp -> CTA
-  Partial p = Op::warp_merge(Op::finish(t, in, head));
+  Partial p = Op::warp_merge(Op::finish(t, head));
   const int warp = threadIdx.x / kWarp;
   const int lane = threadIdx.x % kWarp;
   if (lane == 0) warp_partials[warp] = p;
@@ -328,27 +434,22 @@ __device__ __forceinline__ void reduce_full(const float* __restrict__ in, uint64
 // Kernel entry points.  Parameters use only launch-ABI descriptor codes
 // 10 (device pointer), 3 (u32) and 2 (i32): (in, n_lo, n_hi, out, workspace,
 // index_base_lo, index_base_hi, accumulate).
-extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
-f4s_reduce_sum_f32(const float* in, uint32_t n_lo, uint32_t n_hi, double* out,
-                   unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
-                   int accumulate) {
-  f4s::reduce_full<f4s::SumF32Op>(in, f4s::join_u64(n_lo, n_hi), out, workspace,
-                                  f4s::join_u64(base_lo, base_hi), accumulate);
-}
-
-extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
-f4s_reduce_sum_i32(const int32_t* in, uint32_t n_lo, uint32_t n_hi, int32_t* out,
-                   unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
-                   int accumulate) {
-  f4s::reduce_full<f4s::SumI32Op>(reinterpret_cast<const float*>(in),
-                                  f4s::join_u64(n_lo, n_hi), out, workspace,
-                                  f4s::join_u64(base_lo, base_hi), accumulate);
-}
-
-extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)
-f4s_reduce_argmax_f32(const float* in, uint32_t n_lo, uint32_t n_hi, int64_t* out,
-                      unsigned char* workspace, uint32_t base_lo, uint32_t base_hi,
-                      int accumulate) {
-  f4s::reduce_full<f4s::ArgmaxF32Op>(in, f4s::join_u64(n_lo, n_hi), out, workspace,
-                                     f4s::join_u64(base_lo, base_hi), accumulate);
-}
+#define F4S_REDUCE_KERNEL(NAME, OP)                                                          \
+  extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)                             \
+      NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace, \
+           uint32_t base_lo, uint32_t base_hi, int accumulate) {                              \
+    f4s::reduce_full<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace,                      \
+                         f4s::join_u64(base_lo, base_hi), accumulate);                       \
+  }
+// f32 -> f64 sum; i32 / u32 -> 32-bit wrapping sum; f32 max/argmax
+F4S_REDUCE_KERNEL(f4s_reduce_sum_f32, f4s::SumF32Op)
+F4S_REDUCE_KERNEL(f4s_reduce_sum_i32, f4s::SumWrap32Op)
+F4S_REDUCE_KERNEL(f4s_reduce_argmax_f32, f4s::ArgmaxF32Op)
+// the other AccumulatorType inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
+// accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2
+F4S_REDUCE_KERNEL(f4s_reduce_sum_bf16, f4s::SumHalfOp<true>)
+F4S_REDUCE_KERNEL(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
+F4S_REDUCE_KERNEL(f4s_reduce_sum_f64, f4s::SumF64Op)
+F4S_REDUCE_KERNEL(f4s_reduce_sum_e4m3, f4s::SumFp8Op<true>)
+F4S_REDUCE_KERNEL(f4s_reduce_sum_e5m2, f4s::SumFp8Op<false>)
+#undef F4S_REDUCE_KERNEL

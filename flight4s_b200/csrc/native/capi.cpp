@@ -23,6 +23,8 @@ using flight4s::cuda::CudaDriver;
 using flight4s::cuda::CudaDriverStatus;
 using flight4s::cuda::Hotpath;
 using flight4s::cuda::ReduceOp;
+using flight4s::cuda::kReduceOpCount;
+using flight4s::cuda::sum_op_for_type_code;
 
 struct f4s_hotpath {
   Hotpath* impl;
@@ -407,11 +409,19 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hp, uint64_t stream, uint64_t in, uint64_
   });
 }
 
+int f4s_reduce_sum(f4s_hotpath* hp, uint64_t stream, int32_t input_type, uint64_t in, uint64_t n, uint64_t out,
+                   uint64_t ws, uint64_t ws_bytes, int32_t accumulate) {
+  return guarded([&] {
+    return op_status(
+        hot(hp).reduce(sum_op_for_type_code(input_type), stream_of(stream), in, n, out, ws, ws_bytes, 0, accumulate));
+  });
+}
+
 int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes,
                     uint64_t copy_stream, uint64_t compute_stream) {
   return guarded([&] {
-    if (op < 0 || op > 2) throw std::invalid_argument("unknown reduction op " + std::to_string(op));
+    if (op < 0 || op >= kReduceOpCount) throw std::invalid_argument("unknown reduction op " + std::to_string(op));
     return op_status(hot(hp).reduce_host(static_cast<ReduceOp>(op), host_in, n, index_base, host_out, staging,
                                          staging_bytes, ws, ws_bytes, stream_of(copy_stream),
                                          stream_of(compute_stream)));

@@ -137,6 +137,70 @@ CUfunction Hotpath::function(const std::string& name) const {
   return fn;
 }
 
+namespace {
+
+const char* reduce_kernel_name(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumF32: return "f4s_reduce_sum_f32";
+    case ReduceOp::kSumI32:
+    case ReduceOp::kSumU32: return "f4s_reduce_sum_i32";  // same bits: 32-bit wrap
+    case ReduceOp::kArgmaxF32: return "f4s_reduce_argmax_f32";
+    case ReduceOp::kSumF16: return "f4s_reduce_sum_f16";
+    case ReduceOp::kSumBf16: return "f4s_reduce_sum_bf16";
+    case ReduceOp::kSumF64: return "f4s_reduce_sum_f64";
+    case ReduceOp::kSumE4m3: return "f4s_reduce_sum_e4m3";
+    case ReduceOp::kSumE5m2: return "f4s_reduce_sum_e5m2";
+  }
+  throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
+}
+
+}  // namespace
+
+int reduce_input_bytes(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumF32:
+    case ReduceOp::kSumI32:
+    case ReduceOp::kArgmaxF32:
+    case ReduceOp::kSumU32: return 4;
+    case ReduceOp::kSumF16:
+    case ReduceOp::kSumBf16: return 2;
+    case ReduceOp::kSumF64: return 8;
+    case ReduceOp::kSumE4m3:
+    case ReduceOp::kSumE5m2: return 1;
+  }
+  throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
+}
+
+int reduce_output_bytes(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumI32:
+    case ReduceOp::kSumU32: return 4;
+    case ReduceOp::kArgmaxF32: return 16;
+    case ReduceOp::kSumF32:
+    case ReduceOp::kSumF16:
+    case ReduceOp::kSumBf16:
+    case ReduceOp::kSumF64:
+    case ReduceOp::kSumE4m3:
+    case ReduceOp::kSumE5m2: return 8;  // f64
+  }
+  throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
+}
+
+ReduceOp sum_op_for_type_code(int code) {
+  switch (code) {
+    case 2: return ReduceOp::kSumI32;
+    case 3: return ReduceOp::kSumU32;
+    case 4: return ReduceOp::kSumF16;
+    case 5: return ReduceOp::kSumBf16;
+    case 6: return ReduceOp::kSumF32;
+    case 7: return ReduceOp::kSumF64;
+    case 8: return ReduceOp::kSumE4m3;
+    case 9: return ReduceOp::kSumE5m2;
+    default:
+      throw std::invalid_argument("no ReduceSum accumulator for argument type code " + std::to_string(code));
+  }
+}
+
 CUresult Hotpath::set_reduce_cluster(int cluster) {
   if (cluster < 1 || cluster > 8) throw std::invalid_argument("reduction cluster size must be in [1, 8]");
   const DriverApi& api = require_driver();
@@ -155,9 +219,10 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
   config.attrs = &attr;
   config.numAttrs = 1;
   int clusters = 0;
-  for (const char* name : {"f4s_reduce_sum_f32", "f4s_reduce_sum_i32", "f4s_reduce_argmax_f32"}) {
+  for (int op = 0; op < kReduceOpCount; ++op) {
     int c = 0;
-    const CUresult r = api.cuOccupancyMaxActiveClusters(&c, function(name), &config);
+    const CUresult r =
+        api.cuOccupancyMaxActiveClusters(&c, function(reduce_kernel_name(static_cast<ReduceOp>(op))), &config);
     if (r != CUDA_SUCCESS) return r;
     clusters = clusters == 0 ? c : std::min(clusters, c);
   }
@@ -192,19 +257,22 @@ CUresult Hotpath::launch(CUfunction fn, CUstream stream, int grid, int block, in
 CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
                          CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
                          int accumulate) {
+  const char* name = reduce_kernel_name(op);
+  const int elem = reduce_input_bytes(op);
   if (n > 0) require_ptr(in, "input buffer");
   require_ptr(out, "output buffer");
   require_ptr(workspace, "reduction workspace");
-  if (in % 4 != 0) throw std::invalid_argument("input buffer must be 4-byte aligned");
-  if (op == ReduceOp::kArgmaxF32 && out % 8 != 0)
-    throw std::invalid_argument("argmax output must be 8-byte aligned");
-  if (op == ReduceOp::kSumF32 && out % 8 != 0) throw std::invalid_argument("f64 output must be 8-byte aligned");
+  if (in % elem != 0)
+    throw std::invalid_argument("input buffer must be " + std::to_string(elem) + "-byte aligned");
+  if (reduce_output_bytes(op) >= 8 && out % 8 != 0) throw std::invalid_argument("output must be 8-byte aligned");
+  if (out % 4 != 0) throw std::invalid_argument("output must be 4-byte aligned");
   if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
   const int cluster = shape_.reduce_cluster;
-  // Enough clusters to give each thread >= one unrolled step, at most
-  // kReduceWaves waves of co-resident clusters (several waves measured
-  // faster than one persistent wave: no idle tail).
-  const std::uint64_t per_cluster = static_cast<std::uint64_t>(cluster) * kReduceBlock * 4 * kReduceUnroll;
+  // Enough clusters to give each thread >= one unrolled step of 16-byte
+  // vectors, at most kReduceWaves waves of co-resident clusters (several
+  // waves measured faster than one persistent wave: no idle tail).
+  const std::uint64_t per_cluster =
+      static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * kReduceUnroll;
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
   const int clusters = static_cast<int>(
       std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters) * kReduceWaves));
@@ -213,9 +281,6 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
     throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
                                 " bytes, need " + std::to_string(need));
   }
-  const char* name = op == ReduceOp::kSumF32   ? "f4s_reduce_sum_f32"
-                     : op == ReduceOp::kSumI32 ? "f4s_reduce_sum_i32"
-                                               : "f4s_reduce_argmax_f32";
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
@@ -459,12 +524,12 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
   // staging = [256 B of device-side results (32 B per op) | buffer 0 | buffer 1]
   const std::uint64_t half = ((staging_bytes > 256 ? staging_bytes - 256 : 0) / 2) / 256 * 256;
   if (half < 256) throw std::invalid_argument("staging buffer too small (need >= 768 bytes)");
-  const std::uint64_t chunk = half / 4;  // elements (4-byte types)
+  const int elem = reduce_input_bytes(ops[0]);
+  for (int i = 1; i < nops; ++i)
+    if (reduce_input_bytes(ops[i]) != elem) throw std::invalid_argument("fused host reductions need one input type");
+  const std::uint64_t chunk = half / static_cast<std::uint64_t>(elem);  // elements
   const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
   auto result_slot = [&](int i) { return staging + 32 * static_cast<CUdeviceptr>(i); };
-  auto out_bytes = [](ReduceOp op) -> std::size_t {
-    return op == ReduceOp::kSumF32 ? 8 : op == ReduceOp::kSumI32 ? 4 : 16;
-  };
 
   const DriverApi& api = require_driver();
   Current cur(context_);
@@ -483,7 +548,7 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
     const std::uint64_t count = n == 0 ? 0 : std::min(chunk, n - first);
     if (k >= 2) r = api.cuStreamWaitEvent(copy_stream, consumed[b], 0);
     if (r == CUDA_SUCCESS && count > 0)
-      r = api.cuMemcpyHtoDAsync(buffers[b], static_cast<const unsigned char*>(host_in) + first * 4, count * 4,
+      r = api.cuMemcpyHtoDAsync(buffers[b], static_cast<const unsigned char*>(host_in) + first * elem, count * elem,
                                 copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(copied[b], copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuStreamWaitEvent(compute_stream, copied[b], 0);
@@ -495,7 +560,7 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(consumed[b], compute_stream);
   }
   for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
-    r = api.cuMemcpyDtoHAsync(host_outs[i], result_slot(i), out_bytes(ops[i]), compute_stream);
+    r = api.cuMemcpyDtoHAsync(host_outs[i], result_slot(i), reduce_output_bytes(ops[i]), compute_stream);
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(compute_stream);
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(copy_stream);
   for (int i = 0; i < 2; ++i) {

@@ -22,7 +22,30 @@
 
 namespace flight4s::cuda {
 
-enum class ReduceOp : int { kSumF32 = 0, kSumI32 = 1, kArgmaxF32 = 2 };
+// Full-array reductions.  0..2 are the original f32 / i32 operators; the
+// rest sum the other AccumulatorType inputs of the reference's ReduceSum
+// (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230).
+enum class ReduceOp : int {
+  kSumF32 = 0,
+  kSumI32 = 1,
+  kArgmaxF32 = 2,
+  kSumU32 = 3,
+  kSumF16 = 4,
+  kSumBf16 = 5,
+  kSumF64 = 6,
+  kSumE4m3 = 7,
+  kSumE5m2 = 8,
+};
+constexpr int kReduceOpCount = 9;
+
+// Bytes of one input element and of the result record of `op`.
+int reduce_input_bytes(ReduceOp op);
+int reduce_output_bytes(ReduceOp op);
+// The sum operator for a launch-ABI type code
+// (core/src/main/scala/flight4s/core/abi/CudaAbi.scala:11-20: 2 i32, 3 u32,
+// 4 f16, 5 bf16, 6 f32, 7 f64, 8 fp8 e4m3, 9 fp8 e5m2); throws
+// std::invalid_argument for codes without an accumulator (bool, pointer).
+ReduceOp sum_op_for_type_code(int code);
 
 struct HotpathShape {
   int reduce_cluster = 4;       // CTAs per cluster in the full-array reductions

@@ -16,9 +16,20 @@ from typing import Any, Optional
 import numpy as np
 
 from ._native import check, lib
-from .runtime import CudaContext, CudaModule, device_address, stream_handle
+from .runtime import (BFLOAT16, FLOAT16, FLOAT32, FLOAT64, FP8E4M3, FP8E5M2, INT32, UINT32, CudaContext, CudaModule,
+                      device_address, stream_handle)
 
 REDUCE_SUM_F32, REDUCE_SUM_I32, REDUCE_ARGMAX_F32 = 0, 1, 2
+REDUCE_SUM_U32, REDUCE_SUM_F16, REDUCE_SUM_BF16, REDUCE_SUM_F64, REDUCE_SUM_E4M3, REDUCE_SUM_E5M2 = range(3, 9)
+
+# ReduceSum input types by launch-ABI type code, with each element's size in bytes.
+SUM_TYPE_CODES = {"i32": INT32, "u32": UINT32, "f16": FLOAT16, "bf16": BFLOAT16, "f32": FLOAT32, "f64": FLOAT64,
+                  "e4m3": FP8E4M3, "e5m2": FP8E5M2}
+SUM_TYPE_BYTES = {"i32": 4, "u32": 4, "f16": 2, "bf16": 2, "f32": 4, "f64": 8, "e4m3": 1, "e5m2": 1}
+# f4s_reduce_host op of each input type's sum
+SUM_HOST_OPS = {"f32": REDUCE_SUM_F32, "i32": REDUCE_SUM_I32, "u32": REDUCE_SUM_U32, "f16": REDUCE_SUM_F16,
+                "bf16": REDUCE_SUM_BF16, "f64": REDUCE_SUM_F64, "e4m3": REDUCE_SUM_E4M3, "e5m2": REDUCE_SUM_E5M2}
+_HOST_OP_BYTES = {REDUCE_ARGMAX_F32: 4, **{op: SUM_TYPE_BYTES[t] for t, op in SUM_HOST_OPS.items()}}
 
 # Synthetic distributions of f4s_fill_synthetic
 UNIFORM_F32, UNIFORM_BF16, NORMAL_F32, NORMAL_BF16, UNIFORM_I32, NORMAL_BF16_OUTLIERS = range(6)
@@ -147,6 +158,37 @@ class Hotpath:
             return float("nan"), -1
         return unpack_argmax_key(int(r[0]))[0], index
 
+    def reduce_sum_into(self, dtype: str, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
+                        accumulate: bool = False, workspace: Any = None) -> None:
+        """ReduceSum of any accumulator input type ("i32", "u32", "f16", "bf16",
+        "f32", "f64", "e4m3", "e5m2"): 4-byte wrapping sum for the integer
+        types, f64 for the rest.  Asynchronous."""
+        if dtype not in SUM_TYPE_CODES:
+            raise ValueError(f"no ReduceSum accumulator for {dtype!r}")
+        ws = self.workspace() if workspace is None else workspace
+        check(lib.f4s_reduce_sum(self._h, stream_handle(stream), SUM_TYPE_CODES[dtype], device_address(x),
+                                 _count(x, n), device_address(out), device_address(ws), _nbytes(ws),
+                                 int(accumulate)), f"reduce_sum {dtype}")
+
+    def reduce_sum(self, dtype: str, x: Any, n: Optional[int] = None, stream: Any = None) -> float | int:
+        """Synchronous ReduceSum: int (signed for i32, unsigned for u32) or float."""
+        out = self._result_buffer()
+        self.reduce_sum_into(dtype, x, out, n=n, stream=stream)
+        if stream is not None and hasattr(stream, "synchronize"):
+            stream.synchronize()
+        self.context.synchronize()
+        return self.sum_result(dtype, out.copy_to_array())
+
+    @staticmethod
+    def sum_result(dtype: str, raw: np.ndarray) -> float | int:
+        """Host value of a sum record (the first 8 bytes of `raw`)."""
+        raw = np.ascontiguousarray(raw).view(np.uint8)[:8]
+        if dtype == "i32":
+            return int(raw[:4].view(np.int32)[0])
+        if dtype == "u32":
+            return int(raw[:4].view(np.uint32)[0])
+        return float(raw.view(np.float64)[0])
+
     def reduce_host(self, op: int, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
                     workspace: Any = None, index_base: int = 0) -> np.ndarray:
         """End-to-end reduction of a host array (pinned for overlap) through
@@ -154,6 +196,10 @@ class Hotpath:
         ws = self.workspace() if workspace is None else workspace
         out = np.zeros(2, np.uint64)
         host = np.ascontiguousarray(host)
+        if op not in _HOST_OP_BYTES:
+            raise ValueError(f"unknown reduction op {op}")
+        if host.itemsize != _HOST_OP_BYTES[op]:
+            raise ValueError(f"reduction op {op} reads {_HOST_OP_BYTES[op]}-byte elements, got {host.dtype}")
         check(lib.f4s_reduce_host(self._h, op, host.ctypes.data, host.size, index_base, out.ctypes.data,
                                   device_address(staging), _nbytes(staging), device_address(ws), _nbytes(ws),
                                   stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")

@@ -29,7 +29,7 @@ _ABI = {BOOL8: (1, 1, "?"), INT32: (4, 4, "<i4"), UINT32: (4, 4, "<u4"), FLOAT16
 # element storage types of buffers (bf16 / fp8 are carried as raw bits,
 # like runtime/src/main/scala/flight4s/runtime/cuda/CudaHostCodec.scala:98-128)
 DTYPES = {"f32": np.float32, "f64": np.float64, "i32": np.int32, "u32": np.uint32,
-          "bf16": np.uint16, "f16": np.uint16, "e4m3": np.uint8, "u8": np.uint8, "u64": np.uint64,
+          "bf16": np.uint16, "f16": np.uint16, "e4m3": np.uint8, "e5m2": np.uint8, "u8": np.uint8, "u64": np.uint64,
           "i64": np.int64}
 
 

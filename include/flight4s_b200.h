@@ -226,12 +226,30 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, ui
                           uint64_t workspace, uint64_t workspace_bytes, uint64_t index_base,
                           int32_t accumulate);
 
+/* ReduceSum over every input type the reference accumulates
+ * (AccumulatorType, core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
+ * selected by its launch-ABI type code
+ * (core/src/main/scala/flight4s/core/abi/CudaAbi.scala:11-20):
+ *   2 i32, 3 u32:  *out (4 bytes) = 32-bit two's-complement wrapping sum
+ *                  (bit-exact; the reference accumulates I32 in I32, U32 in U32);
+ *   4 f16, 5 bf16, 6 f32, 8 fp8 e4m3, 9 fp8 e5m2, 7 f64:
+ *                  *out (f64) = sum of the exactly widened inputs, partial
+ *                  sums of each 16-byte vector in f32 (f64 for f64 input),
+ *                  everything above in f64 -- a wider accumulator than the
+ *                  reference's F32 for the 16-bit and 8-bit inputs.
+ * Other codes (1 bool, 10 pointer) return F4S_STATUS_INVALID_ARGUMENT.  `in`
+ * is aligned to its element size.  Code 6 is f4s_reduce_sum_f32 and code 2
+ * f4s_reduce_sum_i32.  One launch; asynchronous on `stream`. */
+int f4s_reduce_sum(f4s_hotpath* hotpath, uint64_t stream, int32_t input_type, uint64_t in, uint64_t n,
+                   uint64_t out, uint64_t workspace, uint64_t workspace_bytes, int32_t accumulate);
+
 /* End-to-end form over a HOST buffer (pinned for overlap): chunked
  * host->device copies on `copy_stream` overlapped with the reduction on
  * `compute_stream` through `staging` (device, >= 768 bytes, 256-aligned),
  * result written to `host_out` (8 / 4 / 16 bytes as above; argmax indices
- * start at `index_base`).  op: 0 sum_f32, 1 sum_i32, 2 argmax_f32.
- * Synchronizes both streams before returning. */
+ * start at `index_base`).  op: 0 sum_f32, 1 sum_i32, 2 argmax_f32,
+ * 3 sum_u32, 4 sum_f16, 5 sum_bf16, 6 sum_f64, 7 sum_e4m3, 8 sum_e5m2
+ * (results as f4s_reduce_sum).  Synchronizes both streams before returning. */
 int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t workspace,
                     uint64_t workspace_bytes, uint64_t copy_stream, uint64_t compute_stream);

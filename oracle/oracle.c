@@ -20,6 +20,10 @@
  *     __NV_SATFINITE/__NV_E4M3 and __float2bfloat16_rn,
  *     core/src/main/scala/flight4s/core/codegen/CudaCodegen.scala:518-538),
  *     run on the host by tests/golden/make_golden_conversions.cpp;
+ *   - the f16, E4M3 and E5M2 decoders (ReduceSum's widening of its 16-bit
+ *     and 8-bit inputs: __half2float and static_cast<float>,
+ *     CudaCodegen.scala:451-466) are pinned on every code against the same
+ *     functions' host forms (tests/golden/decoders.bin.xz);
  *   - max/argmax, softmax, RMSNorm and the FP8 block scaling have no
  *     reference implementation: parity unpinned for those, the oracle is
  *     their definition.
@@ -128,6 +132,44 @@ float orc_e4m3_to_f32(uint8_t c) {
   return (float)(s ? -v : v);
 }
 
+/* ----------------------------------------------------------------- E5M2
+ * OCP 8-bit floating point, E5M2: the IEEE-754 layout with bias 15 and 2
+ * mantissa bits; exponent 31 holds infinities (m == 0) and NaNs. */
+float orc_e5m2_to_f32(uint8_t c) {
+  const int s = c >> 7, e = (c >> 2) & 0x1F, m = c & 3;
+  double v;
+  if (e == 0x1F) v = m ? NAN : INFINITY;
+  else v = e == 0 ? ldexp((double)m, -16) : ldexp(1.0 + m / 4.0, e - 15);
+  return (float)(s ? -v : v);
+}
+
+/* --------------------------------------------------------------- binary16
+ * IEEE-754 binary16: bias 15, 10 mantissa bits, subnormals m * 2^-24,
+ * exponent 31 holds infinities and NaNs.  Widening to f32 is exact. */
+float orc_f16_to_f32(uint16_t h) {
+  const int s = h >> 15, e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  double v;
+  if (e == 0x1F) v = m ? NAN : INFINITY;
+  else v = e == 0 ? ldexp((double)m, -24) : ldexp(1.0 + m / 1024.0, e - 15);
+  return (float)(s ? -v : v);
+}
+
+/* Decode n elements of a ReduceSum input type (launch-ABI type code
+ * 4 f16, 5 bf16, 6 f32, 8 e4m3, 9 e5m2) to f32. */
+int orc_decode_to_f32(int type_code, const void* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    switch (type_code) {
+      case 4: out[i] = orc_f16_to_f32(((const uint16_t*)x)[i]); break;
+      case 5: out[i] = orc_bf16_to_f32(((const uint16_t*)x)[i]); break;
+      case 6: out[i] = ((const float*)x)[i]; break;
+      case 8: out[i] = orc_e4m3_to_f32(((const uint8_t*)x)[i]); break;
+      case 9: out[i] = orc_e5m2_to_f32(((const uint8_t*)x)[i]); break;
+      default: return -1;
+    }
+  }
+  return 0;
+}
+
 /* ----------------------------------------------------------- vectorAdd
  * Array.tabulate(n)(i => l(i) + r(i)) (CudaResourcesJniSuite.scala:120-122). */
 void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n) {
@@ -160,6 +202,41 @@ double orc_sum_f32_exactish(const float* x, int64_t n, double* abs_sum) {
   }
   if (abs_sum) *abs_sum = (double)a;
   return (double)(s + c);
+}
+
+/* Ground truth of a floating-point ReduceSum over any accumulator input
+ * type (launch-ABI code 4 f16, 5 bf16, 6 f32, 7 f64, 8 e4m3, 9 e5m2):
+ * every element widened exactly, then compensated summation in long double.
+ * The reference accumulates the 16-bit and 8-bit types in F32
+ * (core/src/main/scala/flight4s/core/types/CudaType.scala:212-230); this is
+ * the exact value both it and a wider accumulator approximate. */
+double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum) {
+  long double s = 0.0L, c = 0.0L, a = 0.0L;
+  for (int64_t i = 0; i < n; ++i) {
+    long double v;
+    switch (type_code) {
+      case 4: v = orc_f16_to_f32(((const uint16_t*)x)[i]); break;
+      case 5: v = orc_bf16_to_f32(((const uint16_t*)x)[i]); break;
+      case 6: v = ((const float*)x)[i]; break;
+      case 7: v = ((const double*)x)[i]; break;
+      case 8: v = orc_e4m3_to_f32(((const uint8_t*)x)[i]); break;
+      case 9: v = orc_e5m2_to_f32(((const uint8_t*)x)[i]); break;
+      default: return NAN;
+    }
+    const long double t = s + v;
+    if (fabsl(s) >= fabsl(v)) c += (s - t) + v; else c += (v - t) + s;
+    s = t;
+    a += fabsl(v);
+  }
+  if (abs_sum) *abs_sum = (double)a;
+  return (double)(s + c);
+}
+
+/* U32 accumulates in U32 (CudaType.scala:208-210): wrap modulo 2^32. */
+uint32_t orc_sum_u32(const uint32_t* x, int64_t n) {
+  uint32_t acc = 0;
+  for (int64_t i = 0; i < n; ++i) acc += x[i];
+  return acc;
 }
 
 /* I32 accumulates in I32 with two's-complement wrap

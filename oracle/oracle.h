@@ -13,6 +13,11 @@ uint16_t orc_f32_to_bf16_rn(float f);
 float orc_bf16_to_f32(uint16_t b);
 uint8_t orc_f32_to_e4m3_satfinite(float f);
 float orc_e4m3_to_f32(uint8_t c);
+float orc_e5m2_to_f32(uint8_t c);
+float orc_f16_to_f32(uint16_t h);
+int orc_decode_to_f32(int type_code, const void* x, int64_t n, float* out);
+double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum);
+uint32_t orc_sum_u32(const uint32_t* x, int64_t n);
 
 void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n);
 void orc_vector_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n);

@@ -34,6 +34,11 @@ def _load() -> C.CDLL:
         "orc_bf16_to_f32": (C.c_float, [C.c_uint16]),
         "orc_f32_to_e4m3_satfinite": (C.c_uint8, [C.c_float]),
         "orc_e4m3_to_f32": (C.c_float, [C.c_uint8]),
+        "orc_e5m2_to_f32": (C.c_float, [C.c_uint8]),
+        "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
+        "orc_decode_to_f32": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p]),
+        "orc_sum_typed_exactish": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, P(C.c_double)]),
+        "orc_sum_u32": (C.c_uint32, [C.c_void_p, C.c_int64]),
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_sum_f32_sequential": (C.c_float, [C.c_void_p, C.c_int64]),
@@ -134,6 +139,34 @@ def sum_f32_exact(x: np.ndarray) -> tuple[float, float]:
     a = C.c_double()
     s = lib.orc_sum_f32_exactish(_p(x), x.size, C.byref(a))
     return float(s), float(a.value)
+
+
+# launch-ABI type codes (core/src/main/scala/flight4s/core/abi/CudaAbi.scala:11-20)
+TYPE_CODES = {"i32": 2, "u32": 3, "f16": 4, "bf16": 5, "f32": 6, "f64": 7, "e4m3": 8, "e5m2": 9}
+STORAGE = {"i32": np.int32, "u32": np.uint32, "f16": np.uint16, "bf16": np.uint16, "f32": np.float32,
+           "f64": np.float64, "e4m3": np.uint8, "e5m2": np.uint8}
+
+
+def decode_to_f32(dtype: str, x: np.ndarray) -> np.ndarray:
+    """Exact f32 values of f16 / bf16 / f32 / e4m3 / e5m2 storage bits."""
+    x = np.ascontiguousarray(x, STORAGE[dtype])
+    out = np.empty(x.size, np.float32)
+    if lib.orc_decode_to_f32(TYPE_CODES[dtype], _p(x), x.size, _p(out)) != 0:
+        raise ValueError(dtype)
+    return out
+
+
+def sum_typed_exact(dtype: str, x: np.ndarray) -> tuple[float, float]:
+    """(exact sum, sum of |x|) of a floating-point ReduceSum input."""
+    x = np.ascontiguousarray(x, STORAGE[dtype])
+    a = C.c_double()
+    s = lib.orc_sum_typed_exactish(TYPE_CODES[dtype], _p(x), x.size, C.byref(a))
+    return float(s), float(a.value)
+
+
+def sum_u32(x: np.ndarray) -> int:
+    x = np.ascontiguousarray(x, np.uint32)
+    return int(lib.orc_sum_u32(_p(x), x.size))
 
 
 def sum_i32(x: np.ndarray) -> int:

@@ -170,6 +170,28 @@ def hotpath_dispatch():
     hp.reduce_into(f4s.REDUCE_ARGMAX_F32, big, out, n=1000, index_base=(1 << 32) + 5, accumulate=True)
     L = check("f4s_reduce_argmax_f32", 4, block=512, cluster=4)
     assert (param(L, 5, 4), param(L, 6, 4), param(L, 7, 4)) == (5, 1, 1)
+    # typed ReduceSum: kernel per input type, grid sized in 16-byte vectors
+    for dtype, kernel in [("e4m3", "e4m3"), ("e5m2", "e5m2"), ("f16", "f16"), ("bf16", "bf16"), ("f64", "f64"),
+                          ("u32", "i32"), ("i32", "i32"), ("f32", "f32")]:
+        hp.reduce_sum_into(dtype, big, out, n=1000)
+        check(f"f4s_reduce_sum_{kernel}", 4, block=512, cluster=4)
+    hp.reduce_sum_into("e4m3", big, out, n=1 << 20)  # 4 clusters of 4 x 512 x 16 x 8 elements
+    check("f4s_reduce_sum_e4m3", 4 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("f64", big, out, n=1 << 20)   # 2 elements per vector: 32 clusters
+    check("f4s_reduce_sum_f64", 32 * 4, block=512, cluster=4)
+    before = count()
+    ws0 = hp.workspace()
+    for code in (0, 1, 10, 11):   # bool and pointer have no accumulator
+        rc = _native.lib.f4s_reduce_sum(hp.handle, 0, code, big.address, 8, out.address, ws0.address,
+                                        ws0.size_bytes, 0)
+        assert rc == _native.STATUS_INVALID_ARGUMENT and "no ReduceSum accumulator" in _native.last_status()[2]
+    try:
+        hp.reduce_sum_into("f64", big.address + 4, out, n=8)
+    except ValueError as e:
+        assert "8-byte aligned" in str(e)
+    else:
+        raise AssertionError("expected ValueError")
+    assert count() == before
     parts = ctx.allocate("f32", 4096)
     ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
     hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)

@@ -11,13 +11,25 @@
 //               below: u32 fp32 bits, u8 e4m3 code, u16 bf16 bits
 //   exhaustive: compares the oracle's encoders with those functions over all
 //               2^32 fp32 bit patterns and prints the mismatch counts
+//   decoders:   writes the f32 bits (u32 little-endian) of every E4M3 code,
+//               then every E5M2 code, then every f16 code, widened the way
+//               the reference's ReduceSum widens its inputs (__half2float,
+//               static_cast<float> of __nv_fp8_e4m3 / __nv_fp8_e5m2;
+//               CudaCodegen.scala:451-466), NaNs written as 0x7fc00000 (only
+//               NaN-ness is pinned), and prints the oracle decoders' mismatch
+//               count on all 66048 codes
 //
-// Build + run (tests/golden/README in the test that uses it):
+// Build + run (from tests/golden):
+//   gcc -O2 -std=c11 -ffp-contract=off -c ../../oracle/oracle.c -o /tmp/oracle.o
 //   g++ -O2 -std=c++17 -ffp-contract=off -I/usr/local/cuda/include \
-//       make_golden_conversions.cpp ../../oracle/oracle.c -o /tmp/mkconv -lpthread
+//       make_golden_conversions.cpp /tmp/oracle.o -o /tmp/mkconv -lpthread -lm
 //   /tmp/mkconv golden conversions.bin ; /tmp/mkconv exhaustive
+//   /tmp/mkconv decoders /tmp/decoders.bin && xz -9e -c /tmp/decoders.bin > decoders.bin.xz
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
+
+#include <cmath>
 
 #include <cstdint>
 #include <cstdio>
@@ -57,7 +69,50 @@ static std::vector<uint32_t> inputs() {
   return v;
 }
 
+static uint32_t f2u(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+static uint32_t canon(float f) { return std::isnan(f) ? 0x7fc00000u : f2u(f); }
+
+static float cuda_f16(uint16_t bits) {
+  __half_raw raw;
+  raw.x = bits;
+  return __half2float(__half(raw));
+}
+static float cuda_e4m3_dec(uint8_t code) {
+  __nv_fp8_e4m3 v;
+  v.__x = code;
+  return static_cast<float>(v);
+}
+static float cuda_e5m2_dec(uint8_t code) {
+  __nv_fp8_e5m2 v;
+  v.__x = code;
+  return static_cast<float>(v);
+}
+
+static void write_table(FILE* f, unsigned n, float (*dec)(unsigned)) {
+  for (unsigned c = 0; c < n; ++c) {
+    const uint32_t u = canon(dec(c));
+    std::fwrite(&u, 4, 1, f);
+  }
+}
+
 int main(int argc, char** argv) {
+  if (argc >= 3 && std::strcmp(argv[1], "decoders") == 0) {
+    FILE* f = std::fopen(argv[2], "wb");
+    if (!f) return 1;
+    write_table(f, 256, [](unsigned c) { return cuda_e4m3_dec(static_cast<uint8_t>(c)); });
+    write_table(f, 256, [](unsigned c) { return cuda_e5m2_dec(static_cast<uint8_t>(c)); });
+    write_table(f, 65536, [](unsigned c) { return cuda_f16(static_cast<uint16_t>(c)); });
+    std::fclose(f);
+    unsigned bad = 0;
+    for (unsigned c = 0; c < 256; ++c) {
+      bad += canon(orc_e4m3_to_f32(static_cast<uint8_t>(c))) != canon(cuda_e4m3_dec(static_cast<uint8_t>(c)));
+      bad += canon(orc_e5m2_to_f32(static_cast<uint8_t>(c))) != canon(cuda_e5m2_dec(static_cast<uint8_t>(c)));
+    }
+    for (unsigned c = 0; c < 65536; ++c)
+      bad += canon(orc_f16_to_f32(static_cast<uint16_t>(c))) != canon(cuda_f16(static_cast<uint16_t>(c)));
+    std::printf("decoder codes checked: 66048, oracle mismatches: %u\n", bad);
+    return bad == 0 ? 0 : 2;
+  }
   if (argc >= 3 && std::strcmp(argv[1], "golden") == 0) {
     const auto in = inputs();
     FILE* f = std::fopen(argv[2], "wb");
@@ -98,6 +153,6 @@ int main(int argc, char** argv) {
     std::printf("bf16 rn NaN payload differences: %llu\n", (unsigned long long)bn);
     return (e == 0 && b == 0) ? 0 : 2;
   }
-  std::fprintf(stderr, "usage: %s golden <out.bin> | exhaustive\n", argv[0]);
+  std::fprintf(stderr, "usage: %s golden <out.bin> | exhaustive | decoders <out.json>\n", argv[0]);
   return 1;
 }

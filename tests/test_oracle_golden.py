@@ -56,6 +56,39 @@ def test_e4m3_decode_table():
     assert finite.size == 254
 
 
+def _decoder_tables():
+    """Every code widened by CUDA's host conversions (__half2float and
+    static_cast<float> of the FP8 types, as the reference's ReduceSum widens
+    its inputs, CudaCodegen.scala:451-466); NaN canonicalised to 0x7fc00000."""
+    import lzma
+    raw = np.frombuffer(lzma.decompress((GOLDEN / "decoders.bin.xz").read_bytes()), np.uint32)
+    assert raw.size == 256 + 256 + 65536
+    return {"e4m3": raw[:256], "e5m2": raw[256:512], "f16": raw[512:]}
+
+
+def _canonical_bits(f: np.ndarray) -> np.ndarray:
+    bits = f.view(np.uint32).copy()
+    bits[np.isnan(f)] = 0x7FC00000
+    return bits
+
+
+@pytest.mark.parametrize("dtype,codes", [("e4m3", 256), ("e5m2", 256), ("f16", 65536)])
+def test_decoders_match_cuda_conversions_on_every_code(dtype, codes):
+    storage = np.uint8 if codes == 256 else np.uint16
+    ours = orc.decode_to_f32(dtype, np.arange(codes, dtype=storage))
+    golden = _decoder_tables()[dtype]
+    bad = np.nonzero(_canonical_bits(ours) != golden)[0]
+    assert bad.size == 0, [(hex(c), hex(_canonical_bits(ours)[c]), hex(golden[c])) for c in bad[:10]]
+
+
+def test_decoder_tables_known_values():
+    t = {k: v.view(np.float32) for k, v in _decoder_tables().items()}
+    assert t["e5m2"][0x7B] == 57344.0 and t["e5m2"][0x01] == 2.0 ** -16
+    assert np.isinf(t["e5m2"][0x7C]) and np.isnan(t["e5m2"][0x7D])
+    assert t["f16"][0x3C00] == 1.0 and t["f16"][0x7BFF] == 65504.0 and t["f16"][0x0001] == 2.0 ** -24
+    assert np.array_equal(t["e4m3"], orc.E4M3_TABLE, equal_nan=True)
+
+
 def test_philox_known_answer_vectors():
     """Random123 Philox4x32-10 known-answer tests."""
     assert orc.philox([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]

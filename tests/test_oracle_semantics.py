@@ -47,6 +47,30 @@ def test_i32_sum_wraps():
     assert orc.sum_i32(x) == -(2**31) + 5
 
 
+def test_u32_sum_wraps_and_matches_i32_bits():
+    x = np.array([2**32 - 1, 7, 2**31], np.uint32)
+    assert orc.sum_u32(x) == (2**32 - 1 + 7 + 2**31) % 2**32
+    assert orc.sum_u32(x) == orc.sum_i32(x.view(np.int32)) % 2**32
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32", "f64", "e4m3", "e5m2"])
+def test_typed_exact_sum_against_fsum(dtype):
+    rng = np.random.default_rng(3)
+    if dtype in ("e4m3", "e5m2"):
+        x = rng.integers(0, 256, 5000).astype(np.uint8)
+        x = x[np.isfinite(orc.decode_to_f32(dtype, x))]
+    elif dtype in ("f16", "bf16"):
+        x = rng.integers(0, 65536, 5000).astype(np.uint16)
+        x = x[np.isfinite(orc.decode_to_f32(dtype, x))]
+    else:
+        x = (rng.standard_normal(5000) * 1e3).astype(orc.STORAGE[dtype])
+    vals = x.astype(np.float64) if dtype == "f64" else (
+        x.astype(np.float64) if dtype == "f32" else orc.decode_to_f32(dtype, x).astype(np.float64))
+    s, a = orc.sum_typed_exact(dtype, x)
+    assert s == math.fsum(vals)
+    assert a == pytest.approx(float(np.abs(vals).sum()), rel=1e-12)
+
+
 def test_fp8_quantize_properties():
     rows, cols = 4, 384
     rng = np.random.default_rng(3)
