@@ -124,6 +124,42 @@ __device__ __forceinline__ float2 unpack_e5m2x2(uint32_t codes) {
   return make_float2(lo, hi);
 }
 
+// Packed e4m3x2 / e5m2x2 (low 16 bits) -> f16x2, exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t codes) {
+  uint32_t h2;
+  const uint16_t c = static_cast<uint16_t>(codes);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(c));
+  return h2;
+}
+__device__ __forceinline__ uint32_t e5m2x2_to_f16x2(uint32_t codes) {
+  uint32_t h2;
+  const uint16_t c = static_cast<uint16_t>(codes);
+  asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(c));
+  return h2;
+}
+
+// acc + lo + hi for a packed f16x2 / bf16x2 word, with sm_100's
+// mixed-precision add (the 16-bit operand widened exactly; each add rounds
+// once to f32), low half first.
+__device__ __forceinline__ float add_f16x2_to_f32(float acc, uint32_t w) {
+  asm("{.reg .f16 l, h;\n"
+      " mov.b32 {l, h}, %1;\n"
+      " add.rn.f32.f16 %0, l, %0;\n"
+      " add.rn.f32.f16 %0, h, %0;}"
+      : "+f"(acc)
+      : "r"(w));
+  return acc;
+}
+__device__ __forceinline__ float add_bf16x2_to_f32(float acc, uint32_t w) {
+  asm("{.reg .b16 l, h;\n"
+      " mov.b32 {l, h}, %1;\n"
+      " add.rn.f32.bf16 %0, l, %0;\n"
+      " add.rn.f32.bf16 %0, h, %0;}"
+      : "+f"(acc)
+      : "r"(w));
+  return acc;
+}
+
 // IEEE binary16 bits -> f32, exact.
 __device__ __forceinline__ float f16_to_f32(uint16_t h) {
   float f;

@@ -117,55 +117,54 @@ struct SumF32Op : SumF64PartialBase {
   }
 };
 
-// 16-bit floats (bf16 or f16) in, f64 out: the eight elements of a vector
-// are widened exactly to f32 and summed pairwise in f32.
+// 16-bit floats (bf16 or f16) in, f64 out.  Each vector is summed in f32
+// by sm_100's mixed-precision add (add.rn.f32.{f16,bf16}: widen exactly,
+// add, one rounding) in two chains of four elements, then chain + chain;
+// vector sums are combined in f64.
 template <bool kBf16>
 struct SumHalfOp : SumF64PartialBase {
   static constexpr int kElemBytes = 2;
-  static __device__ __forceinline__ float lo(uint32_t w) {
-    if constexpr (kBf16) return bf16_lo(w); else return f16_to_f32(static_cast<uint16_t>(w));
+  static __device__ __forceinline__ float word(float acc, uint32_t w) {
+    if constexpr (kBf16) return add_bf16x2_to_f32(acc, w); else return add_f16x2_to_f32(acc, w);
   }
-  static __device__ __forceinline__ float hi(uint32_t w) {
-    if constexpr (kBf16) return bf16_hi(w); else return f16_to_f32(static_cast<uint16_t>(w >> 16));
-  }
-  static __device__ __forceinline__ float pair(uint32_t w) { return lo(w) + hi(w); }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
     float s[kReduceUnroll];
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
-      s[u] = (u < count) ? (pair(v[u].x) + pair(v[u].y)) + (pair(v[u].z) + pair(v[u].w)) : 0.0f;
+      s[u] = (u < count) ? word(word(0.0f, v[u].x), v[u].y) + word(word(0.0f, v[u].z), v[u].w) : 0.0f;
     }
     t.acc += fold_unrolled_f64(s);
   }
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
     const uint32_t w = static_cast<uint32_t>(bits);
-    t.acc += static_cast<double>(lo(w));
+    t.acc += static_cast<double>(kBf16 ? bf16_lo(w) : f16_to_f32(static_cast<uint16_t>(w)));
   }
 };
 
-// FP8 (E4M3 or E5M2) in, f64 out: sixteen codes per vector, decoded exactly
-// through f16 and summed pairwise in f32 (exact for E4M3); vector sums are
-// combined in f64.
+// FP8 (E4M3 or E5M2) in, f64 out: pairs of codes become f16x2 exactly
+// (cvt.rn.f16x2.{e4m3,e5m2}x2), which the mixed-precision add accumulates in
+// f32 in two chains of eight; every partial sum of E4M3 values is exact in
+// f32 (at most 21 significant bits).  Vector sums are combined in f64.
 template <bool kE4m3>
 struct SumFp8Op : SumF64PartialBase {
   static constexpr int kElemBytes = 1;
-  static __device__ __forceinline__ float2 dec2(uint32_t two_codes) {
-    if constexpr (kE4m3) return unpack_e4m3x2(two_codes); else return unpack_e5m2x2(two_codes);
+  static __device__ __forceinline__ uint32_t to_f16x2(uint32_t two_codes) {
+    if constexpr (kE4m3) return e4m3x2_to_f16x2(two_codes); else return e5m2x2_to_f16x2(two_codes);
   }
-  static __device__ __forceinline__ float quad(uint32_t w) {
-    const float2 a = dec2(w & 0xFFFFu), b = dec2(w >> 16);
-    return (a.x + a.y) + (b.x + b.y);
+  static __device__ __forceinline__ float word(float acc, uint32_t w) {
+    return add_f16x2_to_f32(add_f16x2_to_f32(acc, to_f16x2(w & 0xFFFFu)), to_f16x2(w >> 16));
   }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
     float s[kReduceUnroll];
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
-      s[u] = (u < count) ? (quad(v[u].x) + quad(v[u].y)) + (quad(v[u].z) + quad(v[u].w)) : 0.0f;
+      s[u] = (u < count) ? word(word(0.0f, v[u].x), v[u].y) + word(word(0.0f, v[u].z), v[u].w) : 0.0f;
     }
     t.acc += fold_unrolled_f64(s);
   }
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
-    t.acc += static_cast<double>(dec2(static_cast<uint32_t>(bits) & 0xFFu).x);
+    const uint32_t c = static_cast<uint32_t>(bits) & 0xFFu;
+    t.acc += static_cast<double>(kE4m3 ? unpack_e4m3x2(c).x : unpack_e5m2x2(c).x);
   }
 };
 

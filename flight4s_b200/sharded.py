@@ -8,6 +8,8 @@ small partial, and the partials are combined by one collective:
     sum i32   -> i32 partial (two's-complement),   all_reduce SUM (wraps: bit-exact)
     argmax    -> packed i64 key (signed totalOrder key << 32 | 0xFFFFFFFF - global index),
                                                     all_reduce MAX
+    sum of any other ReduceSum input type (f16, bf16, f64, e4m3, e5m2: f64
+    partial; u32: its 32 bits carried as i32, which wrap identically)
 
 The partial kernels are the hot-path reductions; the collective is
 torch.distributed (NCCL over NVLink on GPUs; gloo in the CPU tests, where
@@ -21,7 +23,7 @@ from typing import Any, Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .hotpath import REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32, unpack_argmax_key
+from .hotpath import REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32, SUM_TYPE_CODES, unpack_argmax_key
 
 MAX_PACKED_INDEX = 0xFFFFFFFF  # packed argmax keys carry 32-bit global indices
 
@@ -44,6 +46,19 @@ def combine_sum_f64(partial: torch.Tensor, group: Any = None) -> torch.Tensor:
 def combine_sum_i32(partial: torch.Tensor, group: Any = None) -> torch.Tensor:
     dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
     return partial
+
+
+def sum_partial_dtype(dtype: str) -> torch.dtype:
+    """Partial (and collective) type of a typed sum: i32 for the 32-bit
+    integer inputs, f64 for the floating-point ones."""
+    if dtype not in SUM_TYPE_CODES:
+        raise ValueError(f"no ReduceSum accumulator for {dtype!r}")
+    return torch.int32 if dtype in ("i32", "u32") else torch.float64
+
+
+def sum_partial_value(dtype: str, partial: torch.Tensor) -> float | int:
+    v = partial.item()
+    return int(v) % (1 << 32) if dtype == "u32" else v
 
 
 def combine_argmax(packed: torch.Tensor, group: Any = None) -> torch.Tensor:
@@ -73,7 +88,8 @@ class ShardedReducer:
         self.i32 = torch.zeros(1, dtype=torch.int32, device=device)
         self.arg = torch.zeros(2, dtype=torch.int64, device=device)
         self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
-        self._pending: dict[int, Any] = {}
+        self.typed: dict[str, torch.Tensor] = {}  # partial of each typed sum
+        self._pending: dict[Any, Any] = {}
 
     @staticmethod
     def _on(stream: Optional[torch.cuda.Stream]):
@@ -81,18 +97,21 @@ class ShardedReducer:
         Work.wait() against the current stream."""
         return torch.cuda.stream(stream) if isinstance(stream, torch.cuda.Stream) else contextlib.nullcontext()
 
-    def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
+    def _release(self, key: Any, shard: torch.Tensor, stream: Optional[torch.cuda.Stream]) -> None:
         if shard.numel() != self.count:
             raise ValueError(f"rank {self.rank} shard holds {shard.numel()} elements, expected {self.count}")
-        prior = self._pending.pop(op, None)
+        prior = self._pending.pop(key, None)
         if prior is not None:
             with self._on(stream):
-                prior.wait()  # the stream waits until that all_reduce has released `out`
+                prior.wait()  # the stream waits until that all_reduce has released the partial
+
+    def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
+        self._release(op, shard, stream)
         self.hp.reduce_into(op, shard, out, n=self.count,
                             stream=stream if stream is not None else torch.cuda.current_stream(),
                             index_base=self.offset, workspace=self.workspace)
 
-    def _combine(self, op: int, tensor: torch.Tensor, reduce_op, stream: Optional[torch.cuda.Stream]) -> None:
+    def _combine(self, op: Any, tensor: torch.Tensor, reduce_op, stream: Optional[torch.cuda.Stream]) -> None:
         if self.world > 1:
             with self._on(stream):
                 self._pending[op] = dist.all_reduce(tensor, op=reduce_op, group=self.group, async_op=True)
@@ -121,6 +140,25 @@ class ShardedReducer:
         self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
         self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
         return self.arg
+
+    def sum_async(self, dtype: str, shard: torch.Tensor, stream=None) -> torch.Tensor:
+        """ReduceSum of any accumulator input type over the sharded array:
+        one kernel on this rank's shard, one all_reduce SUM of the partial."""
+        if dtype not in self.typed:
+            self.typed[dtype] = torch.zeros(1, dtype=sum_partial_dtype(dtype), device=self.device)
+        out = self.typed[dtype]
+        key = ("sum", dtype)
+        self._release(key, shard, stream)
+        self.hp.reduce_sum_into(dtype, shard, out, n=self.count,
+                                stream=stream if stream is not None else torch.cuda.current_stream(),
+                                workspace=self.workspace)
+        self._combine(key, out, dist.ReduceOp.SUM, stream)
+        return out
+
+    def sum(self, dtype: str, shard: torch.Tensor, stream=None) -> float | int:
+        out = self.sum_async(dtype, shard, stream)
+        self.wait(stream)
+        return sum_partial_value(dtype, out)
 
     def sum_f32(self, shard: torch.Tensor, stream=None) -> float:
         self.sum_f32_async(shard, stream)

@@ -38,7 +38,15 @@ def main() -> None:
         red.wait()
         s, i, packed = float(red.f64.item()), int(red.i32.item()), int(red.arg[0].item())
         assert red.sum_i32(xis) == i and red.argmax_f32(xs)[1] >= 0 and red.sum_f32(xs) == s
-        results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed})
+        # typed sums over inputs derived from the i32 data (same derivation in the test)
+        e4m3 = (xis & 0x7E).to(torch.uint8)
+        f16 = (xis & 0x3BFF).to(torch.int16).view(torch.float16)
+        red.sum_async("u32", xis)
+        red.sum_async("e4m3", e4m3)
+        red.sum_async("f16", f16)
+        red.wait()
+        typed = {k: red.sum(k, v) for k, v in (("u32", xis), ("e4m3", e4m3), ("f16", f16))}
+        results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed, "typed": typed})
     torch.cuda.synchronize()
     dist.barrier(device_ids=[local])
     if dist.get_rank() == 0:

@@ -51,3 +51,8 @@ def test_two_gpu_sharded_reductions_match_oracle(tmp_path, n_total):
         assert abs(r["sum_f32"] - exact) <= 1e-5 * abs_sum
         assert r["sum_i32"] == orc.sum_i32(xi)
         assert r["argmax_packed"] == orc.argmax_packed_key(v, idx)
+        t = r["typed"]
+        assert t["u32"] == orc.sum_u32(xi.view(np.uint32))
+        assert t["e4m3"] == orc.sum_typed_exact("e4m3", (xi & 0x7E).astype(np.uint8))[0]  # exact
+        h_exact, h_abs = orc.sum_typed_exact("f16", (xi & 0x3BFF).astype(np.uint16))
+        assert abs(t["f16"] - h_exact) <= 1e-6 * h_abs

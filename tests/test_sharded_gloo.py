@@ -64,6 +64,45 @@ def test_gloo_combine_matches_whole_array(world):
         assert key == orc.argmax_packed_key(v, idx)
 
 
+def _u32_worker(rank: int, world: int, port: int, q):
+    """Typed-sum partials travel as their collective type: u32 bits as i32."""
+    import torch
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    vals = [0xFFFFFFF0, 0x20, 0x7FFFFFFF][:world]
+    t = torch.tensor([vals[rank]], dtype=torch.uint32).view(torch.int32)
+    assert t.dtype == sharded.sum_partial_dtype("u32")
+    sharded.combine_sum_i32(t)
+    q.put((rank, sharded.sum_partial_value("u32", t)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_u32_partials_wrap(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_u32_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = sum([0xFFFFFFF0, 0x20, 0x7FFFFFFF][:world]) % 2**32
+    assert all(v == want for v in results.values())
+
+
+def test_sum_partial_types():
+    import torch
+    assert sharded.sum_partial_dtype("i32") == torch.int32
+    for dtype in ("f16", "bf16", "f32", "f64", "e4m3", "e5m2"):
+        assert sharded.sum_partial_dtype(dtype) == torch.float64
+    with pytest.raises(ValueError):
+        sharded.sum_partial_dtype("bool")
+
+
 def test_shard_bounds_cover_exactly():
     for n in [0, 1, 7, 2**32]:
         for world in [1, 2, 3, 8]:
