@@ -86,6 +86,7 @@ __device__ __forceinline__ double fold_unrolled_f64(const float (&s)[kReduceUnro
 }
 
 struct SumF64PartialBase {
+  static constexpr bool kRolledTail = true;
   using Partial = double;
   struct Thread {
     double acc = 0.0;
@@ -104,6 +105,7 @@ struct SumF64PartialBase {
 // f32 in, f64 out: fp32 pairs inside a 16-byte vector, f64 above.
 struct SumF32Op : SumF64PartialBase {
   static constexpr int kElemBytes = 4;
+  static constexpr bool kRolledTail = false;
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
     float s[kReduceUnroll];
 #pragma unroll
@@ -193,6 +195,7 @@ struct SumF64Op : SumF64PartialBase {
 // i32 or u32 in, 32-bit two's-complement wrap out (bit-identical for both).
 struct SumWrap32Op {
   static constexpr int kElemBytes = 4;
+  static constexpr bool kRolledTail = false;
   using Partial = int32_t;
   struct Thread {
     uint32_t acc = 0;
@@ -229,6 +232,7 @@ struct SumWrap32Op {
 //   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
 struct ArgmaxF32Op {
   static constexpr int kElemBytes = 4;
+  static constexpr bool kRolledTail = false;
   using Partial = ArgmaxPartial;
   struct Thread {
     int32_t vkey = INT32_MIN;  // best key seen in the vector body
@@ -366,13 +370,30 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
     for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_u4(vin + base + u * nthreads);
     Op::body(t, v, base, nthreads, kReduceUnroll);
   }
-  // Fewer than kReduceUnroll vectors left for this thread: one at a time
-  // (a rolled loop keeps the unrolled body's registers free).
+  // Fewer than kReduceUnroll vectors left for this thread.  Ops choose the
+  // form: one unrolled step with a count (argmax measured 12% slower with
+  // the rolled form), or one vector at a time (the unrolled form spills in
+  // the decoding sums).
+  if constexpr (Op::kRolledTail) {
 #pragma unroll 1
-  for (; base < nvec; base += nthreads) {
+    for (; base < nvec; base += nthreads) {
+      uint4 v[kReduceUnroll];
+      v[0] = ld_stream_u4(vin + base);
+      Op::body(t, v, base, nthreads, 1);
+    }
+  } else if (base < nvec) {
     uint4 v[kReduceUnroll];
-    v[0] = ld_stream_u4(vin + base);
-    Op::body(t, v, base, nthreads, 1);
+    int count = 0;
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      if (base + u * nthreads < nvec) {
+        v[u] = ld_stream_u4(vin + base + u * nthreads);
+        count = u + 1;
+      } else {
+        v[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    Op::body(t, v, base, nthreads, count);
   }
 
   // thread -> warp -> CTA

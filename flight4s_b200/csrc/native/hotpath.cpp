@@ -218,17 +218,15 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
   config.blockDimY = config.blockDimZ = 1;
   config.attrs = &attr;
   config.numAttrs = 1;
-  int clusters = 0;
+  int clusters[kReduceOpCount] = {};
   for (int op = 0; op < kReduceOpCount; ++op) {
-    int c = 0;
     const CUresult r =
-        api.cuOccupancyMaxActiveClusters(&c, function(reduce_kernel_name(static_cast<ReduceOp>(op))), &config);
+        api.cuOccupancyMaxActiveClusters(&clusters[op], function(reduce_kernel_name(static_cast<ReduceOp>(op))), &config);
     if (r != CUDA_SUCCESS) return r;
-    clusters = clusters == 0 ? c : std::min(clusters, c);
+    if (clusters[op] <= 0) return CUDA_ERROR_INVALID_CLUSTER_SIZE;
   }
-  if (clusters <= 0) return CUDA_ERROR_INVALID_CLUSTER_SIZE;
   shape_.reduce_cluster = cluster;
-  shape_.reduce_max_clusters = clusters;
+  for (int op = 0; op < kReduceOpCount; ++op) shape_.reduce_max_clusters[op] = clusters[op];
   return scope.close();
 }
 
@@ -275,7 +273,8 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
       static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * kReduceUnroll;
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
   const int clusters = static_cast<int>(
-      std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters) * kReduceWaves));
+      std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters[static_cast<int>(op)]) *
+                                          kReduceWaves));
   const std::uint64_t need = kReducePartialOffset + kReducePartialBytes * static_cast<std::uint64_t>(clusters);
   if (workspace_bytes < need) {
     throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +

@@ -49,7 +49,7 @@ ReduceOp sum_op_for_type_code(int code);
 
 struct HotpathShape {
   int reduce_cluster = 4;       // CTAs per cluster in the full-array reductions
-  int reduce_max_clusters = 0;  // co-resident clusters (occupancy query)
+  int reduce_max_clusters[kReduceOpCount] = {};  // co-resident clusters per op (occupancy query)
   int add_grid = 0;
   int row_ctas_per_sm = 0;
   int fp8_grid = 0;
