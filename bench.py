@@ -440,6 +440,11 @@ def profile_run(which: str) -> None:
         for k in typed:
             rep(lambda: hp.reduce_sum_into(k, raw, out, n=(1 << 30) // f4s.hotpath.SUM_TYPE_BYTES[k]))
         del raw
+    if want("reduce_ordered_f32"):
+        raw = torch.randint(0, 256, (1 << 30,), dtype=torch.uint8, device=dev)
+        out = torch.zeros(2, dtype=torch.int64, device=dev)
+        rep(lambda: hp.reduce_sum_into("f32", raw, out, n=1 << 28, policy="deterministic"))
+        del raw
     if want("vector_add_f32") or want("vector_add_bf16"):
         m = 1 << 26
         for dtype, kind, fn, key in [(torch.float32, f4s.UNIFORM_F32, hp.vector_add_f32, "vector_add_f32"),
@@ -581,6 +586,13 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
         count = (8 << 30) // size
         row(f"reduce_sum_{dtype} 8 GiB", 8 << 30, count,
             timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream), reps=10))
+    # the order-fixed ("deterministic") policy of the same sums
+    for dtype, size in [("f32", 4), ("bf16", 2), ("e4m3", 1)]:
+        count = (8 << 30) // size
+        ws_o = torch.zeros(hp.policy_workspace_bytes(dtype, count, "deterministic"), dtype=torch.uint8, device=dev)
+        row(f"reduce_sum_{dtype} deterministic 8 GiB", 8 << 30, count,
+            timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream, workspace=ws_o,
+                                              policy="deterministic"), reps=10))
     del raw
 
     rows, cols = 32768, 8192

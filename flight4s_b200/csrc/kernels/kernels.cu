@@ -4,6 +4,7 @@
 // its generated kernels (native/src/cuda_driver.cpp:209-261,
 // native/src/cuda_launcher.cpp:8-62).
 #include "reduce.cuh"
+#include "reduce_ordered.cuh"
 #include "block_sum.cuh"
 #include "elementwise.cuh"
 #include "rowwise.cuh"

@@ -24,6 +24,7 @@ using flight4s::cuda::CudaDriverStatus;
 using flight4s::cuda::Hotpath;
 using flight4s::cuda::ReduceOp;
 using flight4s::cuda::kReduceOpCount;
+using flight4s::cuda::ReducePolicy;
 using flight4s::cuda::sum_op_for_type_code;
 
 struct f4s_hotpath {
@@ -414,6 +415,56 @@ int f4s_reduce_sum(f4s_hotpath* hp, uint64_t stream, int32_t input_type, uint64_
   return guarded([&] {
     return op_status(
         hot(hp).reduce(sum_op_for_type_code(input_type), stream_of(stream), in, n, out, ws, ws_bytes, 0, accumulate));
+  });
+}
+
+namespace {
+
+ReducePolicy policy_of(int32_t policy) {
+  if (policy < 0 || policy > 2) throw std::invalid_argument("unknown reduction policy " + std::to_string(policy));
+  return static_cast<ReducePolicy>(policy);
+}
+
+bool uses_ordered(ReduceOp op, ReducePolicy policy) {
+  return policy != ReducePolicy::kFast && Hotpath::has_ordered_kernel(op);
+}
+
+}  // namespace
+
+int f4s_reduce_sum_policy(f4s_hotpath* hp, uint64_t stream, int32_t input_type, int32_t policy, uint64_t in,
+                          uint64_t n, uint64_t out, uint64_t ws, uint64_t ws_bytes, int32_t accumulate) {
+  return guarded([&] {
+    const ReduceOp op = sum_op_for_type_code(input_type);
+    if (uses_ordered(op, policy_of(policy)))
+      return op_status(hot(hp).reduce_ordered(op, stream_of(stream), in, n, out, ws, ws_bytes, accumulate));
+    return op_status(hot(hp).reduce(op, stream_of(stream), in, n, out, ws, ws_bytes, 0, accumulate));
+  });
+}
+
+int f4s_reduce_policy_workspace_bytes(const f4s_hotpath* hp, int32_t input_type, int32_t policy, uint64_t n,
+                                      uint64_t* bytes) {
+  return guarded([&] {
+    if (hp == nullptr || hp->impl == nullptr) throw std::invalid_argument("hotpath handle must not be null");
+    if (bytes == nullptr) throw std::invalid_argument("output pointer must not be null");
+    const ReduceOp op = sum_op_for_type_code(input_type);
+    *bytes = uses_ordered(op, policy_of(policy)) ? Hotpath::ordered_workspace_bytes(op, n)
+                                                 : hp->impl->reduce_workspace_bytes();
+    return 0;
+  });
+}
+
+int f4s_reduce_ordered_groups(int32_t input_type, uint64_t in, uint64_t n, uint64_t* groups) {
+  return guarded([&] {
+    if (groups == nullptr) throw std::invalid_argument("output pointer must not be null");
+    *groups = Hotpath::ordered_groups(sum_op_for_type_code(input_type), in, n);
+    return 0;
+  });
+}
+
+int f4s_reduce_ordered_final(f4s_hotpath* hp, uint64_t stream, uint64_t groups, uint64_t count, uint64_t out,
+                             int32_t accumulate) {
+  return guarded([&] {
+    return op_status(hot(hp).reduce_ordered_final(stream_of(stream), groups, count, out, accumulate));
   });
 }
 

@@ -19,6 +19,9 @@ constexpr int kReduceUnroll = 8;
 constexpr int kReduceWaves = 8;
 constexpr std::uint64_t kReducePartialOffset = 256;
 constexpr std::uint64_t kReducePartialBytes = 16;
+constexpr int kOrderedBlock = 512;
+constexpr std::uint64_t kOrderedGroupBytes = 256 * 1024;  // 64 tiles of 256 16-byte vectors
+constexpr std::uint64_t kOrderedGroupOffset = 256;
 constexpr int kBlockSumThreads = 1024;
 constexpr int kBlockSumCluster = 8;
 constexpr std::int64_t kBlockSumElemsPerCluster = 256LL * 256LL;
@@ -32,6 +35,18 @@ constexpr int kDequantUnroll = 2;
 void check(CUresult r, const char* what) {
   if (r != CUDA_SUCCESS) {
     throw std::runtime_error(std::string(what) + " failed with CUDA error " + std::to_string(r));
+  }
+}
+
+const char* ordered_kernel_name(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumF32: return "f4s_reduce_ordered_f32";
+    case ReduceOp::kSumF16: return "f4s_reduce_ordered_f16";
+    case ReduceOp::kSumBf16: return "f4s_reduce_ordered_bf16";
+    case ReduceOp::kSumF64: return "f4s_reduce_ordered_f64";
+    case ReduceOp::kSumE4m3: return "f4s_reduce_ordered_e4m3";
+    case ReduceOp::kSumE5m2: return "f4s_reduce_ordered_e5m2";
+    default: return nullptr;
   }
 }
 
@@ -86,6 +101,10 @@ Hotpath* Hotpath::open(CUcontext context) {
     hp->shape_.row_ctas_per_sm = occupancy("f4s_softmax_rows_bf16_v4", kRowBlock);
     hp->shape_.fp8_grid = hp->sm_count_ * occupancy("f4s_fp8_quant_flat", kFp8Threads);
     hp->shape_.fill_grid = hp->sm_count_ * occupancy("f4s_fill_synthetic", 256);
+    for (int op = 0; op < kReduceOpCount; ++op) {
+      if (const char* name = ordered_kernel_name(static_cast<ReduceOp>(op)))
+        hp->shape_.ordered_ctas_per_sm[op] = occupancy(name, kOrderedBlock);
+    }
     check(hp->set_reduce_cluster(4), "sizing the reduction grid");
   } catch (...) {
     if (hp->module_ != nullptr) api.cuModuleUnload(hp->module_);
@@ -287,6 +306,62 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
       .u32(static_cast<std::uint32_t>(index_base)).u32(static_cast<std::uint32_t>(index_base >> 32))
       .i32(accumulate ? 1 : 0);
   return cur.finish(launch(function(name), stream, clusters * cluster, kReduceBlock, cluster, args));
+}
+
+bool Hotpath::has_ordered_kernel(ReduceOp op) { return ordered_kernel_name(op) != nullptr; }
+
+std::uint64_t Hotpath::ordered_groups(ReduceOp op, CUdeviceptr in, std::uint64_t n) {
+  if (!has_ordered_kernel(op)) throw std::invalid_argument("no order-fixed kernel for this reduction");
+  const std::uint64_t elem = static_cast<std::uint64_t>(reduce_input_bytes(op));
+  const std::uint64_t head = std::min<std::uint64_t>(((16 - in % 16) % 16) / elem, n);
+  const std::uint64_t body_bytes = (n - head) * elem;
+  return (body_bytes + kOrderedGroupBytes - 1) / kOrderedGroupBytes;
+}
+
+std::uint64_t Hotpath::ordered_workspace_bytes(ReduceOp op, std::uint64_t n) {
+  return kOrderedGroupOffset + 8 * ordered_groups(op, 0, n);
+}
+
+CUresult Hotpath::reduce_ordered(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                                 CUdeviceptr workspace, std::uint64_t workspace_bytes, int accumulate) {
+  const char* name = ordered_kernel_name(op);
+  if (name == nullptr) throw std::invalid_argument("no order-fixed kernel for this reduction");
+  const int elem = reduce_input_bytes(op);
+  if (n > 0) require_ptr(in, "input buffer");
+  require_ptr(out, "output buffer");
+  require_ptr(workspace, "reduction workspace");
+  if (in % elem != 0)
+    throw std::invalid_argument("input buffer must be " + std::to_string(elem) + "-byte aligned");
+  if (out % 8 != 0) throw std::invalid_argument("output must be 8-byte aligned");
+  if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
+  const std::uint64_t groups = ordered_groups(op, in, n);
+  const std::uint64_t need = kOrderedGroupOffset + 8 * groups;
+  if (workspace_bytes < need) {
+    throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
+                                " bytes, need " + std::to_string(need));
+  }
+  const std::uint64_t resident =
+      static_cast<std::uint64_t>(sm_count_) * static_cast<std::uint64_t>(shape_.ordered_ctas_per_sm[static_cast<int>(op)]);
+  const int grid = static_cast<int>(std::max<std::uint64_t>(1, std::min<std::uint64_t>(groups, resident)));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32)).ptr(out).ptr(workspace)
+      .i32(accumulate ? 1 : 0);
+  return cur.finish(launch(function(name), stream, grid, kOrderedBlock, 0, args));
+}
+
+CUresult Hotpath::reduce_ordered_final(CUstream stream, CUdeviceptr groups, std::uint64_t count, CUdeviceptr out,
+                                       int accumulate) {
+  if (count > 0) require_ptr(groups, "group partials");
+  require_ptr(out, "output buffer");
+  if (groups % 8 != 0 || out % 8 != 0) throw std::invalid_argument("group partials and output must be 8-byte aligned");
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(groups).u32(static_cast<std::uint32_t>(count)).u32(static_cast<std::uint32_t>(count >> 32)).ptr(out)
+      .i32(accumulate ? 1 : 0);
+  return cur.finish(launch(function("f4s_reduce_ordered_final"), stream, 1, kOrderedBlock, 0, args));
 }
 
 CUresult Hotpath::block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,

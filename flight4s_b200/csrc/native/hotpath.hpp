@@ -47,6 +47,14 @@ int reduce_output_bytes(ReduceOp op);
 // std::invalid_argument for codes without an accumulator (bool, pointer).
 ReduceOp sum_op_for_type_code(int code);
 
+// The reference's ReductionPolicy (core/src/main/scala/flight4s/core/ir/IR.scala:79-82).
+// Fast: the geometry-sized kernels (reproducible on one device and launch
+// shape).  Deterministic and Strict: the order-fixed kernels, whose
+// floating-point result depends on the elements only (any grid, cluster,
+// device or GPU count); the reference's serial loop order itself cannot be
+// kept by a parallel sum, so Strict gets the same fixed order.
+enum class ReducePolicy : int { kStrict = 0, kDeterministic = 1, kFast = 2 };
+
 struct HotpathShape {
   int reduce_cluster = 4;       // CTAs per cluster in the full-array reductions
   int reduce_max_clusters[kReduceOpCount] = {};  // co-resident clusters per op (occupancy query)
@@ -54,6 +62,7 @@ struct HotpathShape {
   int row_ctas_per_sm = 0;
   int fp8_grid = 0;
   int fill_grid = 0;
+  int ordered_ctas_per_sm[kReduceOpCount] = {};  // order-fixed sums (float ops only)
 };
 
 class Hotpath {
@@ -75,6 +84,19 @@ class Hotpath {
   CUresult reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
                   CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
                   int accumulate);
+  // Order-fixed floating-point sums: 256 KiB groups of the 16-byte-aligned
+  // body, group partials in `workspace` from byte 256 (f64 each, readable
+  // after the launch), total = fixed tree over the group partials + the
+  // unaligned head.  f32/f16/bf16/f64/e4m3/e5m2 sum ops only.
+  static bool has_ordered_kernel(ReduceOp op);
+  static std::uint64_t ordered_groups(ReduceOp op, CUdeviceptr in, std::uint64_t n);
+  static std::uint64_t ordered_workspace_bytes(ReduceOp op, std::uint64_t n);  // any alignment
+  CUresult reduce_ordered(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                          CUdeviceptr workspace, std::uint64_t workspace_bytes, int accumulate);
+  // The same fixed tree over `count` group partials (several GPUs' partials
+  // concatenated in array order).
+  CUresult reduce_ordered_final(CUstream stream, CUdeviceptr groups, std::uint64_t count, CUdeviceptr out,
+                                int accumulate);
   CUresult block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,
                          CUdeviceptr out, CUdeviceptr workspace, std::uint64_t workspace_bytes);
   CUresult vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,

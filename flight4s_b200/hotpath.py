@@ -31,6 +31,11 @@ SUM_HOST_OPS = {"f32": REDUCE_SUM_F32, "i32": REDUCE_SUM_I32, "u32": REDUCE_SUM_
                 "bf16": REDUCE_SUM_BF16, "f64": REDUCE_SUM_F64, "e4m3": REDUCE_SUM_E4M3, "e5m2": REDUCE_SUM_E5M2}
 _HOST_OP_BYTES = {REDUCE_ARGMAX_F32: 4, **{op: SUM_TYPE_BYTES[t] for t, op in SUM_HOST_OPS.items()}}
 
+# ReductionPolicy of the reference's ReduceSum (core/src/main/scala/flight4s/core/ir/IR.scala:79-82)
+POLICIES = {"strict": 0, "deterministic": 1, "fast": 2}
+ORDERED_TYPES = ("f16", "bf16", "f32", "f64", "e4m3", "e5m2")
+ORDERED_GROUP_BYTES = 256 * 1024  # order-fixed sums: one f64 partial per 256 KiB group
+
 # Synthetic distributions of f4s_fill_synthetic
 UNIFORM_F32, UNIFORM_BF16, NORMAL_F32, NORMAL_BF16, UNIFORM_I32, NORMAL_BF16_OUTLIERS = range(6)
 
@@ -73,6 +78,7 @@ class Hotpath:
         self.module = CudaModule(context, lib.f4s_hotpath_module(h), owned=False)
         self.workspace_bytes = int(lib.f4s_reduce_workspace_bytes(h))
         self._workspace = None
+        self._ordered_workspace = None
         self._result = None
 
     # ------------------------------------------------------------ plumbing
@@ -92,6 +98,31 @@ class Hotpath:
         ws = self.context.allocate("u8", self.workspace_bytes)
         ws.copy_from(np.zeros(self.workspace_bytes, np.uint8))
         return ws
+
+    def policy_workspace_bytes(self, dtype: str, n: int, policy: str = "fast") -> int:
+        """Workspace bytes a ReduceSum of `n` elements needs under `policy`."""
+        b = C.c_uint64()
+        check(lib.f4s_reduce_policy_workspace_bytes(self._h, SUM_TYPE_CODES[dtype], POLICIES[policy], int(n),
+                                                    C.byref(b)), "policy workspace size")
+        return int(b.value)
+
+    def ordered_workspace(self, nbytes: int):
+        """Zeroed workspace of at least `nbytes` for order-fixed sums, kept and
+        grown by this hotpath (same stream rule as `workspace`)."""
+        if self._ordered_workspace is None or self._ordered_workspace.size_bytes < nbytes:
+            if self._ordered_workspace is not None:
+                self._ordered_workspace.close()
+            self._ordered_workspace = self.context.allocate("u8", nbytes)
+            self._ordered_workspace.copy_from(np.zeros(nbytes, np.uint8))
+        return self._ordered_workspace
+
+    @staticmethod
+    def ordered_groups(dtype: str, address: int, n: int) -> int:
+        """Group partials an order-fixed sum of `n` elements at `address` writes."""
+        g = C.c_uint64()
+        check(lib.f4s_reduce_ordered_groups(SUM_TYPE_CODES[dtype], int(address), int(n), C.byref(g)),
+              "ordered group count")
+        return int(g.value)
 
     def _result_buffer(self):
         if self._result is None:
@@ -114,7 +145,7 @@ class Hotpath:
 
     def close(self) -> None:
         if self._h is not None:
-            for b in (self._workspace, self._result):
+            for b in (self._workspace, self._ordered_workspace, self._result):
                 if b is not None:
                     b.close()
             check(lib.f4s_hotpath_close(self._h), "hot-path module unload")
@@ -159,21 +190,39 @@ class Hotpath:
         return unpack_argmax_key(int(r[0]))[0], index
 
     def reduce_sum_into(self, dtype: str, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
-                        accumulate: bool = False, workspace: Any = None) -> None:
+                        accumulate: bool = False, workspace: Any = None, policy: str = "fast") -> None:
         """ReduceSum of any accumulator input type ("i32", "u32", "f16", "bf16",
         "f32", "f64", "e4m3", "e5m2"): 4-byte wrapping sum for the integer
-        types, f64 for the rest.  Asynchronous."""
+        types, f64 for the rest.  `policy` "strict" / "deterministic" selects
+        the order-fixed kernels for floating-point inputs (the same bits on
+        any launch shape, device or GPU count), "fast" the geometry-sized
+        ones.  Asynchronous."""
         if dtype not in SUM_TYPE_CODES:
             raise ValueError(f"no ReduceSum accumulator for {dtype!r}")
-        ws = self.workspace() if workspace is None else workspace
-        check(lib.f4s_reduce_sum(self._h, stream_handle(stream), SUM_TYPE_CODES[dtype], device_address(x),
-                                 _count(x, n), device_address(out), device_address(ws), _nbytes(ws),
-                                 int(accumulate)), f"reduce_sum {dtype}")
+        if policy not in POLICIES:
+            raise ValueError(f"unknown reduction policy {policy!r}")
+        count = _count(x, n)
+        if workspace is not None:
+            ws = workspace
+        elif policy != "fast" and dtype in ORDERED_TYPES:
+            ws = self.ordered_workspace(self.policy_workspace_bytes(dtype, count, policy))
+        else:
+            ws = self.workspace()
+        check(lib.f4s_reduce_sum_policy(self._h, stream_handle(stream), SUM_TYPE_CODES[dtype], POLICIES[policy],
+                                        device_address(x), count, device_address(out), device_address(ws),
+                                        _nbytes(ws), int(accumulate)), f"reduce_sum {dtype} ({policy})")
 
-    def reduce_sum(self, dtype: str, x: Any, n: Optional[int] = None, stream: Any = None) -> float | int:
+    def reduce_ordered_final_into(self, groups: Any, count: int, out: Any, stream: Any = None,
+                                  accumulate: bool = False) -> None:
+        """Order-fixed total of `count` f64 group partials (device memory)."""
+        check(lib.f4s_reduce_ordered_final(self._h, stream_handle(stream), device_address(groups), int(count),
+                                           device_address(out), int(accumulate)), "reduce_ordered_final")
+
+    def reduce_sum(self, dtype: str, x: Any, n: Optional[int] = None, stream: Any = None,
+                   policy: str = "fast") -> float | int:
         """Synchronous ReduceSum: int (signed for i32, unsigned for u32) or float."""
         out = self._result_buffer()
-        self.reduce_sum_into(dtype, x, out, n=n, stream=stream)
+        self.reduce_sum_into(dtype, x, out, n=n, stream=stream, policy=policy)
         if stream is not None and hasattr(stream, "synchronize"):
             stream.synchronize()
         self.context.synchronize()

@@ -23,19 +23,35 @@ from typing import Any, Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .hotpath import REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32, SUM_TYPE_CODES, unpack_argmax_key
+from .hotpath import (ORDERED_GROUP_BYTES, ORDERED_TYPES, POLICIES, REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32,
+                      SUM_TYPE_BYTES, SUM_TYPE_CODES, unpack_argmax_key)
 
 MAX_PACKED_INDEX = 0xFFFFFFFF  # packed argmax keys carry 32-bit global indices
 
 
-def shard_bounds(n_total: int, world: int, rank: int) -> tuple[int, int]:
-    """Contiguous shard of rank `rank`: [offset, offset + count).  The first
-    n_total % world ranks take one extra element."""
+# Shard granule (elements) for order-fixed sums: a multiple of every input
+# type's 256 KiB group, so each GPU holds whole groups.
+ORDERED_GRANULE = 1 << 18
+
+
+def shard_bounds(n_total: int, world: int, rank: int, granule: int = 1) -> tuple[int, int]:
+    """Contiguous shard of rank `rank`: [offset, offset + count).  With
+    granule 1 the first n_total % world ranks take one extra element; with a
+    larger granule every shard but the last non-empty one is a whole number
+    of granules (ceil(units / world) each), so only trailing ranks are short."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
-    base, extra = divmod(n_total, world)
-    offset = rank * base + min(rank, extra)
-    return offset, base + (1 if rank < extra else 0)
+    if granule < 1:
+        raise ValueError("granule must be >= 1")
+    if granule == 1:
+        base, extra = divmod(n_total, world)
+        offset = rank * base + min(rank, extra)
+        return offset, base + (1 if rank < extra else 0)
+    units = -(-n_total // granule)
+    per = -(-units // world)
+    lo = min(rank * per * granule, n_total)
+    hi = min((rank + 1) * per * granule, n_total)
+    return lo, hi - lo
 
 
 def combine_sum_f64(partial: torch.Tensor, group: Any = None) -> torch.Tensor:
@@ -76,19 +92,23 @@ class ShardedReducer:
     for that buffer's previous all_reduce.  Call `wait()` (device-side) before
     reading results on `stream`; the `*_result` helpers do so."""
 
-    def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None):
+    def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None, granule: int = 1):
         self.hp = hotpath
         self.device = device
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.n_total = n_total
-        self.offset, self.count = shard_bounds(n_total, self.world, self.rank)
+        self.granule = granule
+        self.offset, self.count = shard_bounds(n_total, self.world, self.rank, granule)
+        self.counts = [shard_bounds(n_total, self.world, r, granule)[1] for r in range(self.world)]
         self.f64 = torch.zeros(1, dtype=torch.float64, device=device)
         self.i32 = torch.zeros(1, dtype=torch.int32, device=device)
         self.arg = torch.zeros(2, dtype=torch.int64, device=device)
         self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
         self.typed: dict[str, torch.Tensor] = {}  # partial of each typed sum
+        self._ordered: dict[str, dict[str, torch.Tensor]] = {}  # per-type buffers of order-fixed sums
+        self._ordered_groups: dict[str, int] = {}  # this rank's group count per type
         self._pending: dict[Any, Any] = {}
 
     @staticmethod
@@ -141,9 +161,62 @@ class ShardedReducer:
         self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
         return self.arg
 
-    def sum_async(self, dtype: str, shard: torch.Tensor, stream=None) -> torch.Tensor:
+    def _ordered_buffers(self, dtype: str) -> dict[str, torch.Tensor]:
+        """Workspace, local / gathered group partials and result of an
+        order-fixed sum of `dtype` (allocated on first use)."""
+        if dtype not in self._ordered:
+            itemsize = SUM_TYPE_BYTES[dtype]
+            per_group = ORDERED_GROUP_BYTES // itemsize
+            groups = [-(-c // per_group) for c in self.counts]
+            m = max(max(groups), 1)
+            ws_bytes = self.hp.policy_workspace_bytes(dtype, self.count, "deterministic")
+            self._ordered[dtype] = {
+                "ws": torch.zeros(ws_bytes, dtype=torch.uint8, device=self.device),
+                "local": torch.zeros(m, dtype=torch.float64, device=self.device),
+                "gathered": torch.zeros(m * self.world, dtype=torch.float64, device=self.device),
+                "out": torch.zeros(1, dtype=torch.float64, device=self.device),
+            }
+            self._ordered_groups[dtype] = groups[self.rank]
+        return self._ordered[dtype]
+
+    def _sum_ordered_async(self, dtype: str, shard: torch.Tensor, policy: str, stream) -> torch.Tensor:
+        """Order-fixed sum over the GPUs: each rank writes its shard's group
+        partials, one all_gather concatenates them in array order, and every
+        rank runs the same final tree -- the same bits as one GPU."""
+        itemsize = SUM_TYPE_BYTES[dtype]
+        if (self.offset * itemsize) % ORDERED_GROUP_BYTES or shard.data_ptr() % 16:
+            raise ValueError("order-fixed sharded sums need 16-byte-aligned shards of whole 256 KiB groups "
+                             f"(construct the reducer with granule={ORDERED_GRANULE})")
+        b = self._ordered_buffers(dtype)
+        key = ("ordered", dtype)
+        self._release(key, shard, stream)
+        s = stream if stream is not None else torch.cuda.current_stream()
+        with self._on(stream):
+            self.hp.reduce_sum_into(dtype, shard, b["out"], n=self.count, stream=s, workspace=b["ws"], policy=policy)
+            ng = self._ordered_groups[dtype]
+            b["local"].zero_()
+            b["local"][:ng].copy_(b["ws"][256:256 + 8 * ng].view(torch.float64))
+            dist.all_gather_into_tensor(b["gathered"], b["local"], group=self.group)
+            self.hp.reduce_ordered_final_into(b["gathered"], b["gathered"].numel(), b["out"], stream=s)
+        return b["out"]
+
+    def sum_async(self, dtype: str, shard: torch.Tensor, stream=None, policy: str = "fast") -> torch.Tensor:
         """ReduceSum of any accumulator input type over the sharded array:
-        one kernel on this rank's shard, one all_reduce SUM of the partial."""
+        one kernel on this rank's shard, one all_reduce SUM of the partial.
+        policy "deterministic" / "strict" (floating-point inputs): the
+        order-fixed sum, bit-identical to one GPU's (needs granule-aligned
+        shards)."""
+        if policy not in POLICIES:
+            raise ValueError(f"unknown reduction policy {policy!r}")
+        if policy != "fast" and dtype in ORDERED_TYPES and self.world > 1:
+            return self._sum_ordered_async(dtype, shard, policy, stream)
+        if policy != "fast" and dtype in ORDERED_TYPES:
+            b = self._ordered_buffers(dtype)
+            self._release(("ordered", dtype), shard, stream)
+            self.hp.reduce_sum_into(dtype, shard, b["out"], n=self.count,
+                                    stream=stream if stream is not None else torch.cuda.current_stream(),
+                                    workspace=b["ws"], policy=policy)
+            return b["out"]
         if dtype not in self.typed:
             self.typed[dtype] = torch.zeros(1, dtype=sum_partial_dtype(dtype), device=self.device)
         out = self.typed[dtype]
@@ -155,8 +228,8 @@ class ShardedReducer:
         self._combine(key, out, dist.ReduceOp.SUM, stream)
         return out
 
-    def sum(self, dtype: str, shard: torch.Tensor, stream=None) -> float | int:
-        out = self.sum_async(dtype, shard, stream)
+    def sum(self, dtype: str, shard: torch.Tensor, stream=None, policy: str = "fast") -> float | int:
+        out = self.sum_async(dtype, shard, stream, policy)
         self.wait(stream)
         return sum_partial_value(dtype, out)
 

@@ -243,6 +243,38 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, ui
 int f4s_reduce_sum(f4s_hotpath* hotpath, uint64_t stream, int32_t input_type, uint64_t in, uint64_t n,
                    uint64_t out, uint64_t workspace, uint64_t workspace_bytes, int32_t accumulate);
 
+/* ReduceSum under the reference's ReductionPolicy
+ * (core/src/main/scala/flight4s/core/ir/IR.scala:79-82): 0 Strict,
+ * 1 Deterministic, 2 Fast.
+ *   Fast: f4s_reduce_sum (partial sums associated by launch geometry:
+ *         reproducible for one device and launch shape).
+ *   Strict, Deterministic, floating-point inputs (f16 bf16 f32 f64 e4m3
+ *         e5m2): order-fixed kernels.  The body (from the first 16-byte
+ *         boundary) is cut into 256 KiB groups; every group's f64 partial is
+ *         a fixed tree over its elements, the total is a fixed tree over the
+ *         group partials plus the unaligned head elements in order.  The
+ *         result depends on the elements and the 16-byte phase of `in`
+ *         only: the same bits on any grid, cluster size, B200 or number of
+ *         GPUs holding whole groups (f4s_reduce_ordered_final).  The
+ *         reference's Strict names its serial loop's order, which no parallel
+ *         sum keeps; Strict gets the same fixed order as Deterministic.
+ *   Integer inputs are exact under every policy (Fast kernel).
+ * The workspace needed depends on the policy and n:
+ * f4s_reduce_policy_workspace_bytes.  Group partials (f64) stay readable in
+ * the workspace from byte 256 after an order-fixed launch. */
+int f4s_reduce_sum_policy(f4s_hotpath* hotpath, uint64_t stream, int32_t input_type, int32_t policy, uint64_t in,
+                          uint64_t n, uint64_t out, uint64_t workspace, uint64_t workspace_bytes,
+                          int32_t accumulate);
+int f4s_reduce_policy_workspace_bytes(const f4s_hotpath* hotpath, int32_t input_type, int32_t policy, uint64_t n,
+                                      uint64_t* bytes);
+/* Number of 256 KiB group partials an order-fixed sum of in[0, n) writes. */
+int f4s_reduce_ordered_groups(int32_t input_type, uint64_t in, uint64_t n, uint64_t* groups);
+/* *out (f64) = the order-fixed total of `count` group partials (f64, device
+ * memory), e.g. the partials of several GPUs' shards concatenated in array
+ * order.  One launch; asynchronous on `stream`. */
+int f4s_reduce_ordered_final(f4s_hotpath* hotpath, uint64_t stream, uint64_t groups, uint64_t count, uint64_t out,
+                             int32_t accumulate);
+
 /* End-to-end form over a HOST buffer (pinned for overlap): chunked
  * host->device copies on `copy_stream` overlapped with the reduction on
  * `compute_stream` through `staging` (device, >= 768 bytes, 256-aligned),

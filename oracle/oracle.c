@@ -232,6 +232,138 @@ double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* a
   return (double)(s + c);
 }
 
+/* ------------------------------------------------- order-fixed sums
+ * The order-fixed ("Deterministic") sum the B200 kernels define for the
+ * reference's ReductionPolicy (core/src/main/scala/flight4s/core/ir/IR.scala:79-82),
+ * restated operation by operation so results compare bit for bit:
+ *   body = elements from the first 16-byte boundary (`head` elements before
+ *   it), cut into 16-byte vectors (the last zero-padded); tile = 256
+ *   vectors, lane l of 32 takes vectors l + 32u (u < 8); group = 64 tiles.
+ *   vector value: f32 (a+b)+(c+d); f16/bf16 ((((0+h0)+h1)+h2)+h3) +
+ *   ((((0+h4)+h5)+h6)+h7) in f32; FP8 the same over bytes 0..7 and 8..15;
+ *   f64 d0+d1.  Lane: the 8 vector values (zero past the end) folded
+ *   pairwise (s0+=s1, s2+=s3, ...; s0+=s2, ...; s0+=s4) -- in f32 then
+ *   widened for f32 input, in f64 otherwise -- added to 0.0.  Tile: warp
+ *   tree v[l] += v[l+o], o = 16..1.  Group: the warp tree of
+ *   tile[l] + tile[l+32].  Total: thread t of 512 adds groups t, t+512, ...
+ *   in order from 0.0; warp trees; the 16 warp values (16 zeros after
+ *   them) through one more warp tree; then + the head elements, each widened
+ *   and added in order to 0.0. */
+static int elem_bytes(int type_code) {
+  switch (type_code) {
+    case 4: case 5: return 2;
+    case 6: return 4;
+    case 7: return 8;
+    case 8: case 9: return 1;
+    default: return 0;
+  }
+}
+
+static double widen(int type_code, const unsigned char* p) {
+  switch (type_code) {
+    case 4: { uint16_t h; memcpy(&h, p, 2); return orc_f16_to_f32(h); }
+    case 5: { uint16_t h; memcpy(&h, p, 2); return orc_bf16_to_f32(h); }
+    case 6: { float f; memcpy(&f, p, 4); return f; }
+    case 7: { double d; memcpy(&d, p, 8); return d; }
+    case 8: return orc_e4m3_to_f32(*p);
+    default: return orc_e5m2_to_f32(*p);
+  }
+}
+
+static float widen_f(int type_code, const unsigned char* p) { return (float)widen(type_code, p); }
+
+/* value of one 16-byte vector; f32-valued types return the f32 widened */
+static double vector_value(int type_code, const unsigned char* v, int* is_f32) {
+  *is_f32 = type_code != 7;
+  if (type_code == 6) {
+    const float a = widen_f(6, v), b = widen_f(6, v + 4), c = widen_f(6, v + 8), d = widen_f(6, v + 12);
+    return (double)((a + b) + (c + d));
+  }
+  if (type_code == 7) return widen(7, v) + widen(7, v + 8);
+  const int eb = elem_bytes(type_code), half = 8 / eb;
+  float a = 0.0f, b = 0.0f;
+  for (int k = 0; k < half; ++k) a = a + widen_f(type_code, v + k * eb);
+  for (int k = 0; k < half; ++k) b = b + widen_f(type_code, v + 8 + k * eb);
+  return (double)(a + b);
+}
+
+static double warp_tree(double* v) {
+  for (int o = 16; o > 0; o >>= 1)
+    for (int l = 0; l < o; ++l) v[l] = v[l] + v[l + o];
+  return v[0];
+}
+
+double orc_ordered_final(const double* groups, int64_t count) {
+  double acc[512], warps[32];
+  for (int t = 0; t < 512; ++t) {
+    double a = 0.0;
+    for (int64_t g = t; g < count; g += 512) a = a + groups[g];
+    acc[t] = a;
+  }
+  for (int w = 0; w < 16; ++w) warps[w] = warp_tree(acc + 32 * w);
+  for (int w = 16; w < 32; ++w) warps[w] = 0.0;
+  return warp_tree(warps);
+}
+
+double orc_sum_ordered(int type_code, const void* x, int64_t n, int64_t head, double* groups_out,
+                       int64_t* ngroups_out) {
+  const int eb = elem_bytes(type_code);
+  if (eb == 0 || head < 0 || head > n) return NAN;
+  const unsigned char* in = (const unsigned char*)x;
+  const unsigned char* body = in + head * eb;
+  const int per = 16 / eb;
+  const int64_t nvec_full = (n - head) / per;
+  const int tail = (int)((n - head) % per);
+  const int64_t nvec = nvec_full + (tail > 0);
+  const int64_t ntiles = (nvec + 255) / 256, ngroups = (ntiles + 63) / 64;
+  unsigned char tailv[16];
+  memset(tailv, 0, 16);
+  if (tail > 0) memcpy(tailv, body + nvec_full * 16, (size_t)tail * eb);
+  double* groups = (double*)malloc(sizeof(double) * (size_t)(ngroups > 0 ? ngroups : 1));
+  for (int64_t g = 0; g < ngroups; ++g) {
+    double tiles[64];
+    for (int local = 0; local < 64; ++local) {
+      const int64_t tile = g * 64 + local;
+      double lanes[32];
+      for (int l = 0; l < 32; ++l) {
+        double sd[8];
+        float sf[8];
+        int is_f32 = 1;
+        for (int u = 0; u < 8; ++u) {
+          const int64_t idx = tile * 256 + l + 32 * u;
+          double val = 0.0;
+          if (tile < ntiles && idx < nvec) val = vector_value(type_code, idx < nvec_full ? body + idx * 16 : tailv, &is_f32);
+          sd[u] = val;
+          sf[u] = (float)val;
+        }
+        double folded;
+        if (type_code == 6) {
+          for (int w = 1; w < 8; w <<= 1)
+            for (int u = 0; u + w < 8; u += 2 * w) sf[u] = sf[u] + sf[u + w];
+          folded = (double)sf[0];
+        } else {
+          for (int w = 1; w < 8; w <<= 1)
+            for (int u = 0; u + w < 8; u += 2 * w) sd[u] = sd[u] + sd[u + w];
+          folded = sd[0];
+        }
+        lanes[l] = tile < ntiles ? 0.0 + folded : 0.0;
+      }
+      tiles[local] = warp_tree(lanes);
+    }
+    double v[32];
+    for (int l = 0; l < 32; ++l) v[l] = tiles[l] + tiles[l + 32];
+    groups[g] = warp_tree(v);
+  }
+  double total = orc_ordered_final(groups, ngroups);
+  double h = 0.0;
+  for (int64_t i = 0; i < head; ++i) h = h + widen(type_code, in + i * eb);
+  total = total + h;
+  if (groups_out) memcpy(groups_out, groups, sizeof(double) * (size_t)ngroups);
+  if (ngroups_out) *ngroups_out = ngroups;
+  free(groups);
+  return total;
+}
+
 /* U32 accumulates in U32 (CudaType.scala:208-210): wrap modulo 2^32. */
 uint32_t orc_sum_u32(const uint32_t* x, int64_t n) {
   uint32_t acc = 0;

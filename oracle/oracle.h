@@ -18,6 +18,9 @@ float orc_f16_to_f32(uint16_t h);
 int orc_decode_to_f32(int type_code, const void* x, int64_t n, float* out);
 double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum);
 uint32_t orc_sum_u32(const uint32_t* x, int64_t n);
+double orc_ordered_final(const double* groups, int64_t count);
+double orc_sum_ordered(int type_code, const void* x, int64_t n, int64_t head, double* groups_out,
+                       int64_t* ngroups_out);
 
 void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n);
 void orc_vector_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n);

@@ -39,6 +39,8 @@ def _load() -> C.CDLL:
         "orc_decode_to_f32": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p]),
         "orc_sum_typed_exactish": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, P(C.c_double)]),
         "orc_sum_u32": (C.c_uint32, [C.c_void_p, C.c_int64]),
+        "orc_ordered_final": (C.c_double, [C.c_void_p, C.c_int64]),
+        "orc_sum_ordered": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, P(C.c_int64)]),
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_sum_f32_sequential": (C.c_float, [C.c_void_p, C.c_int64]),
@@ -162,6 +164,23 @@ def sum_typed_exact(dtype: str, x: np.ndarray) -> tuple[float, float]:
     a = C.c_double()
     s = lib.orc_sum_typed_exactish(TYPE_CODES[dtype], _p(x), x.size, C.byref(a))
     return float(s), float(a.value)
+
+
+def sum_ordered(dtype: str, x: np.ndarray, head: int = 0) -> tuple[float, np.ndarray]:
+    """Order-fixed sum (bit-exact restatement of the device kernels) of x,
+    whose first `head` elements lie before the first 16-byte boundary;
+    returns (total, group partials)."""
+    x = np.ascontiguousarray(x, STORAGE[dtype])
+    ng = C.c_int64()
+    size = (x.size * x.itemsize + (1 << 18) - 1) >> 18
+    groups = np.zeros(max(size, 1), np.float64)
+    total = lib.orc_sum_ordered(TYPE_CODES[dtype], _p(x), x.size, head, _p(groups), C.byref(ng))
+    return float(total), groups[:ng.value]
+
+
+def ordered_final(groups: np.ndarray) -> float:
+    g = np.ascontiguousarray(groups, np.float64)
+    return float(lib.orc_ordered_final(_p(g), g.size))
 
 
 def sum_u32(x: np.ndarray) -> int:

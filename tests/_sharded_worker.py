@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 
 import flight4s_b200 as f4s
-from flight4s_b200.sharded import ShardedReducer
+from flight4s_b200.sharded import ORDERED_GRANULE, ShardedReducer
 
 
 def main() -> None:
@@ -47,10 +47,21 @@ def main() -> None:
         red.wait()
         typed = {k: red.sum(k, v) for k, v in (("u32", xis), ("e4m3", e4m3), ("f16", f16))}
         results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed, "typed": typed})
+    # order-fixed sums over granule-aligned shards: the same bits as one GPU
+    red_o = ShardedReducer(hp, dev, n_total, granule=ORDERED_GRANULE)
+    xo = torch.empty(max(red_o.count, 1), dtype=torch.float32, device=dev)
+    hp.fill_synthetic(xo, red_o.count, f4s.UNIFORM_F32, seed=99, offset=red_o.offset)
+    xos = xo[:red_o.count]
+    xob = xos.to(torch.bfloat16)
+    ordered = []
+    for _ in range(2):
+        ordered.append({"f32": red_o.sum("f32", xos, policy="deterministic"),
+                        "bf16": red_o.sum("bf16", xob, policy="strict")})
     torch.cuda.synchronize()
     dist.barrier(device_ids=[local])
     if dist.get_rank() == 0:
-        Path(out_path).write_text(json.dumps({"world": dist.get_world_size(), "results": results}))
+        Path(out_path).write_text(json.dumps({"world": dist.get_world_size(), "results": results,
+                                              "ordered": ordered}))
     ctx.close()
     dist.destroy_process_group()
 

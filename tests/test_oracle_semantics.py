@@ -98,3 +98,35 @@ def test_softmax_and_rmsnorm_definitions():
     w = orc.f32_to_bf16(np.ones(cols, np.float32))
     r = orc.rmsnorm_rows(x, w, rows, cols, 1e-6)
     assert np.allclose((r ** 2).mean(axis=1), 1.0, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32", "f64", "e4m3", "e5m2"])
+def test_ordered_sum_definition(dtype):
+    """The order-fixed sum: close to the exact sum, its total is the fixed
+    final tree of its group partials, and whole groups of a shard have the
+    same partials as in the full array (what makes multi-GPU results equal)."""
+    rng = np.random.default_rng(9)
+    eb = np.dtype(orc.STORAGE[dtype]).itemsize
+    group = (256 * 1024) // eb
+    n = 3 * group + 12345
+    if dtype in ("e4m3", "e5m2"):
+        x = rng.integers(0, 256, n + n // 4).astype(np.uint8)
+        x = x[np.isfinite(orc.decode_to_f32(dtype, x))][:n]
+    elif dtype == "f16":
+        x = (rng.standard_normal(n) * 100).astype(np.float16).view(np.uint16)
+    elif dtype == "bf16":
+        x = orc.f32_to_bf16((rng.standard_normal(n) * 100).astype(np.float32))
+    else:
+        x = rng.standard_normal(n).astype(orc.STORAGE[dtype])
+    total, groups = orc.sum_ordered(dtype, x)
+    exact, abs_sum = orc.sum_typed_exact(dtype, x)
+    assert abs(total - exact) <= 1e-6 * abs_sum
+    assert groups.size == 4 and orc.ordered_final(groups) == total
+    t2, g2 = orc.sum_ordered(dtype, x[group:])
+    assert np.array_equal(g2, groups[1:])
+    # trailing zero partials (padding of a short last shard) change nothing
+    assert orc.ordered_final(np.concatenate([groups, np.zeros(5)])) == total
+    # a misaligned start moves the head elements out of the body
+    th, gh = orc.sum_ordered(dtype, x, head=min(3, 16 // eb - 1))
+    assert abs(th - exact) <= 1e-6 * abs_sum
+
