@@ -86,7 +86,6 @@ __device__ __forceinline__ double fold_unrolled_f64(const float (&s)[kReduceUnro
 }
 
 struct SumF64PartialBase {
-  static constexpr bool kRolledTail = true;
   using Partial = double;
   struct Thread {
     double acc = 0.0;
@@ -105,7 +104,6 @@ struct SumF64PartialBase {
 // f32 in, f64 out: fp32 pairs inside a 16-byte vector, f64 above.
 struct SumF32Op : SumF64PartialBase {
   static constexpr int kElemBytes = 4;
-  static constexpr bool kRolledTail = false;
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
     float s[kReduceUnroll];
 #pragma unroll
@@ -195,7 +193,6 @@ struct SumF64Op : SumF64PartialBase {
 // i32 or u32 in, 32-bit two's-complement wrap out (bit-identical for both).
 struct SumWrap32Op {
   static constexpr int kElemBytes = 4;
-  static constexpr bool kRolledTail = false;
   using Partial = int32_t;
   struct Thread {
     uint32_t acc = 0;
@@ -232,7 +229,6 @@ struct SumWrap32Op {
 //   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
 struct ArgmaxF32Op {
   static constexpr int kElemBytes = 4;
-  static constexpr bool kRolledTail = false;
   using Partial = ArgmaxPartial;
   struct Thread {
     int32_t vkey = INT32_MIN;  // best key seen in the vector body
@@ -361,39 +357,38 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
   for (uint64_t i = tail_begin + tid; i < n; i += nthreads)
     Op::scalar(t, load_element_bits<kElem>(in + i * kElem), i);
 
+  // Body in warp tiles of 256 vectors (4 KiB): lane l of a warp loads
+  // vectors l + 32u (u < kReduceUnroll) of its tile, so each warp streams
+  // 4 KiB of contiguous memory per step; warps stride over the tiles.
+  // (Measured against a thread-strided layout: equal for f32/i32/argmax,
+  // +10% for the bf16 and FP8 sums.)  Each lane still sees its vectors in
+  // increasing index order.
   const uint4* vin = reinterpret_cast<const uint4*>(in + head * kElem);
-  const uint64_t step = nthreads * kReduceUnroll;
-  uint64_t base = tid;
-  for (; base + (kReduceUnroll - 1) * nthreads < nvec; base += step) {
+  const uint64_t tile_lane = threadIdx.x % kWarp;
+  const uint64_t nwarps = nthreads / kWarp;
+  const uint64_t full_tiles = nvec / (kWarp * kReduceUnroll);
+  uint64_t tile = tid / kWarp;
+  for (; tile < full_tiles; tile += nwarps) {
+    const uint64_t base = tile * (kWarp * kReduceUnroll) + tile_lane;
     uint4 v[kReduceUnroll];
 #pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_u4(vin + base + u * nthreads);
-    Op::body(t, v, base, nthreads, kReduceUnroll);
+    for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld_stream_u4(vin + base + u * kWarp);
+    Op::body(t, v, base, kWarp, kReduceUnroll);
   }
-  // Fewer than kReduceUnroll vectors left for this thread.  Ops choose the
-  // form: one unrolled step with a count (argmax measured 12% slower with
-  // the rolled form), or one vector at a time (the unrolled form spills in
-  // the decoding sums).
-  if constexpr (Op::kRolledTail) {
-#pragma unroll 1
-    for (; base < nvec; base += nthreads) {
-      uint4 v[kReduceUnroll];
-      v[0] = ld_stream_u4(vin + base);
-      Op::body(t, v, base, nthreads, 1);
-    }
-  } else if (base < nvec) {
+  if (tile == full_tiles) {  // exactly one warp owns the partial last tile
+    const uint64_t base = tile * (kWarp * kReduceUnroll) + tile_lane;
     uint4 v[kReduceUnroll];
     int count = 0;
 #pragma unroll
     for (int u = 0; u < kReduceUnroll; ++u) {
-      if (base + u * nthreads < nvec) {
-        v[u] = ld_stream_u4(vin + base + u * nthreads);
+      if (base + u * kWarp < nvec) {
+        v[u] = ld_stream_u4(vin + base + u * kWarp);
         count = u + 1;
       } else {
         v[u] = make_uint4(0, 0, 0, 0);
       }
     }
-    Op::body(t, v, base, nthreads, count);
+    if (count > 0) Op::body(t, v, base, kWarp, count);
   }
 
   // thread -> warp -> CTA
