@@ -184,7 +184,7 @@ class ShardedReducer:
         partials, one all_gather concatenates them in array order, and every
         rank runs the same final tree -- the same bits as one GPU."""
         itemsize = SUM_TYPE_BYTES[dtype]
-        if (self.offset * itemsize) % ORDERED_GROUP_BYTES or shard.data_ptr() % 16:
+        if self.count and ((self.offset * itemsize) % ORDERED_GROUP_BYTES or shard.data_ptr() % 16):
             raise ValueError("order-fixed sharded sums need 16-byte-aligned shards of whole 256 KiB groups "
                              f"(construct the reducer with granule={ORDERED_GRANULE})")
         b = self._ordered_buffers(dtype)
