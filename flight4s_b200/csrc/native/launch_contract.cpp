@@ -21,6 +21,7 @@ std::optional<DescriptorLayout> descriptor_layout(std::int8_t code) {
       return DescriptorLayout{4, 4};
     case kFloat64:
     case kDevicePointer64:
+    case kSignedInt64:
       return DescriptorLayout{8, 8};
     default:
       return std::nullopt;

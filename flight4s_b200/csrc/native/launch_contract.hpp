@@ -50,6 +50,9 @@ enum DescriptorCode : std::int8_t {
   kFloat8E4M3 = 8,
   kFloat8E5M2 = 9,
   kDevicePointer64 = 10,
+  // Addition (not one of the reference's codes): a signed 64-bit value, so
+  // element counts and offsets above 2^31 - 1 pass as one argument.
+  kSignedInt64 = 11,
 };
 
 struct DescriptorLayout {
@@ -72,6 +75,7 @@ class ArgumentPack {
  public:
   ArgumentPack& ptr(std::uint64_t device_address) { return put(kDevicePointer64, &device_address); }
   ArgumentPack& i32(std::int32_t v) { return put(kSignedInt32, &v); }
+  ArgumentPack& i64(std::int64_t v) { return put(kSignedInt64, &v); }
   ArgumentPack& u32(std::uint32_t v) { return put(kUnsignedInt32, &v); }
   ArgumentPack& f32(float v) { return put(kFloat32, &v); }
   ArgumentPack& f64(double v) { return put(kFloat64, &v); }

@@ -22,9 +22,11 @@ from ._native import CudaDriverFailure, check, lib
 # --------------------------------------------------------------- ABI codes
 # core/src/main/scala/flight4s/core/abi/CudaAbi.scala:12-21
 BOOL8, INT32, UINT32, FLOAT16, BFLOAT16, FLOAT32, FLOAT64, FP8E4M3, FP8E5M2, DEVPTR = range(1, 11)
+# Addition: signed 64-bit values (element counts / offsets beyond 2^31 - 1)
+INT64 = 11
 _ABI = {BOOL8: (1, 1, "?"), INT32: (4, 4, "<i4"), UINT32: (4, 4, "<u4"), FLOAT16: (2, 2, "<u2"),
         BFLOAT16: (2, 2, "<u2"), FLOAT32: (4, 4, "<f4"), FLOAT64: (8, 8, "<f8"), FP8E4M3: (1, 1, "u1"),
-        FP8E5M2: (1, 1, "u1"), DEVPTR: (8, 8, "<u8")}
+        FP8E5M2: (1, 1, "u1"), DEVPTR: (8, 8, "<u8"), INT64: (8, 8, "<i8")}
 
 # element storage types of buffers (bf16 / fp8 are carried as raw bits,
 # like runtime/src/main/scala/flight4s/runtime/cuda/CudaHostCodec.scala:98-128)

@@ -76,7 +76,13 @@ int f4s_driver_available(void);
  * (native/include/flight4s/cuda/launch_contract.hpp:35-42,
  * native/src/launch_contract.cpp:49-199).  Return 0 when valid, else
  * F4S_STATUS_INVALID_ARGUMENT with the reference's message in
- * f4s_last_status_description().  Pure host code: no driver needed. */
+ * f4s_last_status_description().  Pure host code: no driver needed.
+ * Descriptor codes are the reference's 1..10 (1 bool, 2 i32, 3 u32, 4 f16,
+ * 5 bf16, 6 f32, 7 f64, 8 e4m3, 9 e5m2, 10 device pointer;
+ * core/src/main/scala/flight4s/core/abi/CudaAbi.scala:11-20) plus one
+ * addition, 11 = signed 64-bit integer (8 bytes, 8-aligned), for element
+ * counts and offsets above 2^31 - 1; every other code is rejected with the
+ * reference's message. */
 int f4s_validate_launch_geometry(int32_t grid_x, int32_t grid_y, int32_t grid_z, int32_t block_x,
                                  int32_t block_y, int32_t block_z, int32_t dynamic_shared_memory_bytes,
                                  int32_t uses_cluster, int32_t cluster_x, int32_t cluster_y,

@@ -112,11 +112,13 @@ def test_randomised_layouts_match_reference_contract():
             elif defect == 2:
                 size += int(rng.choice([-1, 1, 8]))
             elif defect == 3 and k:
-                codes[int(rng.integers(0, k))] = int(rng.choice([0, 11, 127, -1]))
+                codes[int(rng.integers(0, k))] = int(rng.choice([0, 12, 127, -1]))
             elif defect == 4:
                 misalign = int(rng.choice([1, 2, 4]))
         else:
-            codes = [int(c) for c in rng.choice([1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 0, 11, 127], size=k)]
+            # code 11 is this library's one addition (signed 64-bit); the
+            # reference rejects it, so it is compared separately below
+            codes = [int(c) for c in rng.choice([1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 0, 12, 127], size=k)]
             offsets = sorted(int(o) for o in rng.integers(-2, 48, size=k))
             n_codes = k if rng.random() > 0.1 else max(k - 1, 0)
             size = int(rng.integers(-1, 64))
@@ -133,6 +135,22 @@ def test_randomised_layouts_match_reference_contract():
     mismatches = [(c, a, b) for c, a, b in zip(cases, ours, ref) if a != b]
     assert not mismatches, mismatches[:5]
     assert sum(v == "OK" for v in ref) > 20 and sum(v != "OK" for v in ref) > 1000
+
+
+def test_signed_int64_code_is_the_one_addition():
+    """Code 11 (signed 64-bit, 8 bytes, 8-aligned) validates and packs here;
+    the reference's contract rejects it as unknown, and both agree on 12."""
+    storage = (C.c_uint64 * 3)()
+    assert _ours_layout(C.addressof(storage), 24, [0, 8, 16], [2, 11, 10])[0] == 0
+    assert "not aligned to 8 bytes" in _ours_layout(C.addressof(storage), 16, [0, 4], [2, 11])[1]
+    assert "unknown descriptor code" in _ours_layout(C.addressof(storage), 16, [0, 8], [2, 12])[1]
+    packed = f4s.NativeArgumentStorage([(f4s.INT32, 7), (f4s.INT64, (1 << 40) + 3), (f4s.DEVPTR, 0x1000)])
+    assert list(packed.offsets)[:3] == [0, 8, 16] and packed.size_bytes == 24
+    raw = (C.c_uint8 * 24).from_address(packed.address)
+    assert np.frombuffer(bytes(raw[8:16]), np.int64)[0] == (1 << 40) + 3
+    ref = orc.reference_contract_check(["L 24 0 0 3 3 0 8 16 2 11 10", "L 16 0 0 2 2 0 8 2 12"])
+    if ref is not None:
+        assert ref[0] != "OK" and ref[1] != "OK"
 
 
 def test_reference_contract_test_cases():

@@ -53,6 +53,41 @@ def test_ptx_module_ordinary_and_clustered_launch(ctx):
     module.close()
 
 
+# Hand-written PTX taking a signed 64-bit argument (descriptor code 11):
+# out[i] = start + i for i < 4, start passed as one 64-bit value.
+WRITE_I64_PTX = b"""
+.version 8.7
+.target sm_100a
+.address_size 64
+.visible .entry write_i64(.param .u64 out, .param .u32 tag, .param .s64 start)
+{
+  .reg .b32 %r<3>;
+  .reg .b64 %rd<6>;
+  ld.param.u64 %rd1, [out];
+  ld.param.s64 %rd2, [start];
+  mov.u32 %r1, %tid.x;
+  cvt.s64.u32 %rd3, %r1;
+  add.s64 %rd4, %rd2, %rd3;
+  cvta.to.global.u64 %rd5, %rd1;
+  mul.wide.u32 %rd3, %r1, 8;
+  add.s64 %rd5, %rd5, %rd3;
+  st.global.s64 [%rd5], %rd4;
+  ret;
+}
+"""
+
+
+def test_signed_int64_argument_launch(ctx):
+    module = ctx.load_ptx(WRITE_I64_PTX)
+    fn = module.function("write_i64", signature=[f4s.DEVPTR, f4s.UINT32, f4s.INT64])
+    out = ctx.allocate("i64", 4)
+    start = (1 << 40) - 2
+    fn.launch(fn.bind(out, 5, start), f4s.LaunchConfig(f4s.Grid(1), f4s.Block(4)))
+    ctx.synchronize()
+    assert out.copy_to_array().tolist() == [start + i for i in range(4)]
+    module.close()
+
+
 def test_ptx_with_nul_byte_is_rejected(ctx):
     with pytest.raises(ValueError, match="null byte"):
         ctx.load_ptx(b".version 8.7\x00")
