@@ -445,6 +445,16 @@ def profile_run(which: str) -> None:
         out = torch.zeros(2, dtype=torch.int64, device=dev)
         rep(lambda: hp.reduce_sum_into("f32", raw, out, n=1 << 28, policy="deterministic"))
         del raw
+    if want("convert"):
+        m = 1 << 26
+        xf = torch.empty(m, dtype=torch.float32, device=dev)
+        hp.fill_synthetic(xf, m, f4s.NORMAL_F32, seed=SEED, p0=0.0, p1=100.0)
+        h16 = torch.empty(m, dtype=torch.uint16, device=dev)
+        q8 = torch.empty(m, dtype=torch.uint8, device=dev)
+        rep(lambda: hp.convert_into("f32", "bf16", xf, h16))
+        rep(lambda: hp.convert_into("f32", "e4m3", xf, q8))
+        rep(lambda: hp.convert_into("e4m3", "f32", q8, xf))
+        del xf, h16, q8
     if want("vector_add_f32") or want("vector_add_bf16"):
         m = 1 << 26
         for dtype, kind, fn, key in [(torch.float32, f4s.UNIFORM_F32, hp.vector_add_f32, "vector_add_f32"),
@@ -594,6 +604,22 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
             timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream, workspace=ws_o,
                                               policy="deterministic"), reps=10))
     del raw
+
+    # elementwise Convert, 2^28 elements (f32 side 1 GiB)
+    n = 1 << 28
+    xf = torch.empty(n, dtype=torch.float32, device=dev)
+    hp.fill_synthetic(xf, n, f4s.NORMAL_F32, seed=SEED, p0=0.0, p1=100.0)
+    h16 = torch.empty(n, dtype=torch.uint16, device=dev)
+    q8 = torch.empty(n, dtype=torch.uint8, device=dev)
+    yf = torch.empty_like(xf)
+    row("convert f32->bf16 rn n=2^28", 6 * n, n, timeit(lambda: hp.convert_into("f32", "bf16", xf, h16, stream=stream)))
+    row("convert f32->f16 rz n=2^28", 6 * n, n,
+        timeit(lambda: hp.convert_into("f32", "f16", xf, h16, rounding="toward_zero", stream=stream)))
+    row("convert f32->e4m3 satfinite n=2^28", 5 * n, n,
+        timeit(lambda: hp.convert_into("f32", "e4m3", xf, q8, stream=stream)))
+    row("convert e4m3->f32 n=2^28", 5 * n, n, timeit(lambda: hp.convert_into("e4m3", "f32", q8, yf, stream=stream)))
+    row("convert f16->f32 n=2^28", 6 * n, n, timeit(lambda: hp.convert_into("f16", "f32", h16, yf, stream=stream)))
+    del xf, h16, q8, yf
 
     rows, cols = 32768, 8192
     xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)

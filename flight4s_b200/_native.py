@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "f4s_reduce_policy_workspace_bytes": (C.c_int, [vp, i32, i32, u64, P(u64)]),
     "f4s_reduce_ordered_groups": (C.c_int, [i32, u64, u64, P(u64)]),
     "f4s_reduce_ordered_final": (C.c_int, [vp, u64, u64, u64, u64, i32]),
+    "f4s_convert": (C.c_int, [vp, u64, i32, i32, i32, i32, u64, u64, u64]),
     "f4s_reduce_host": (C.c_int, [vp, i32, vp, u64, u64, vp, u64, u64, u64, u64, u64, u64]),
     "f4s_reduce_host_sum_argmax_f32": (C.c_int, [vp, vp, u64, u64, vp, vp, u64, u64, u64, u64, u64, u64]),
     "f4s_block_reduce_workspace_bytes": (u64, [i32]),

@@ -9,4 +9,5 @@
 #include "elementwise.cuh"
 #include "rowwise.cuh"
 #include "fp8.cuh"
+#include "convert.cuh"
 #include "synthetic.cuh"

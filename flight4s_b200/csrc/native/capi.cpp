@@ -468,6 +468,13 @@ int f4s_reduce_ordered_final(f4s_hotpath* hp, uint64_t stream, uint64_t groups, 
   });
 }
 
+int f4s_convert(f4s_hotpath* hp, uint64_t stream, int32_t from_type, int32_t to_type, int32_t rounding,
+                int32_t saturation, uint64_t in, uint64_t out, uint64_t n) {
+  return guarded([&] {
+    return op_status(hot(hp).convert(stream_of(stream), from_type, to_type, rounding, saturation, in, out, n));
+  });
+}
+
 int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes,
                     uint64_t copy_stream, uint64_t compute_stream) {

@@ -2,6 +2,7 @@
 
 #include <algorithm>
 #include <stdexcept>
+#include <string>
 
 #include "cuda_launcher.hpp"
 #include "launch_contract.hpp"
@@ -306,6 +307,80 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
       .u32(static_cast<std::uint32_t>(index_base)).u32(static_cast<std::uint32_t>(index_base >> 32))
       .i32(accumulate ? 1 : 0);
   return cur.finish(launch(function(name), stream, clusters * cluster, kReduceBlock, cluster, args));
+}
+
+namespace {
+
+// Bytes and the reference's CUDA spelling of each launch-ABI type that
+// Convert can name (core/src/main/scala/flight4s/core/types/CudaType.scala:60-140).
+int type_bytes(int code) {
+  switch (code) {
+    case 1: case 8: case 9: return 1;
+    case 4: case 5: return 2;
+    case 2: case 3: case 6: return 4;
+    case 7: return 8;
+    default: return 0;
+  }
+}
+
+const char* cuda_type_name(int code) {
+  switch (code) {
+    case 1: return "bool";
+    case 2: return "int";
+    case 3: return "unsigned int";
+    case 4: return "__half";
+    case 5: return "__nv_bfloat16";
+    case 6: return "float";
+    case 7: return "double";
+    case 8: return "__nv_fp8_e4m3";
+    case 9: return "__nv_fp8_e5m2";
+    default: return nullptr;
+  }
+}
+
+std::string convert_kernel_name(int from, int to, int rounding, int saturation) {
+  if (cuda_type_name(from) == nullptr || cuda_type_name(to) == nullptr)
+    throw std::invalid_argument("unknown Convert type code " + std::to_string(cuda_type_name(from) ? to : from));
+  if (rounding < 0 || rounding > 3) throw std::invalid_argument("unknown rounding mode " + std::to_string(rounding));
+  if (saturation < 0 || saturation > 1)
+    throw std::invalid_argument("unknown saturation mode " + std::to_string(saturation));
+  static const char* const kRound[] = {"rn", "rz", "ru", "rd"};
+  if (from == to) return "f4s_convert_copy_" + std::to_string(type_bytes(from));
+  if (from == 6 && to == 4) return std::string("f4s_convert_f32_f16_") + kRound[rounding];
+  if (from == 6 && to == 5) return std::string("f4s_convert_f32_bf16_") + kRound[rounding];
+  // FP8 conversion rounds to nearest-even whatever the mode (the reference's
+  // lowering passes no rounding to __nv_cvt_float_to_fp8)
+  if (from == 6 && to == 8) return saturation ? "f4s_convert_f32_e4m3_sat" : "f4s_convert_f32_e4m3_nosat";
+  if (from == 6 && to == 9) return saturation ? "f4s_convert_f32_e5m2_sat" : "f4s_convert_f32_e5m2_nosat";
+  if (to == 6 && from == 4) return "f4s_convert_f16_f32";
+  if (to == 6 && from == 5) return "f4s_convert_bf16_f32";
+  if (to == 6 && from == 8) return "f4s_convert_e4m3_f32";
+  if (to == 6 && from == 9) return "f4s_convert_e5m2_f32";
+  // CudaCodegen.scala:440-449 (UnsupportedConversion, CudaArtifacts.scala:84-91)
+  throw std::invalid_argument(std::string("cannot emit a conversion from ") + cuda_type_name(from) + " to " +
+                              cuda_type_name(to));
+}
+
+}  // namespace
+
+CUresult Hotpath::convert(CUstream stream, int from_type, int to_type, int rounding, int saturation, CUdeviceptr in,
+                          CUdeviceptr out, std::uint64_t n) {
+  const std::string name = convert_kernel_name(from_type, to_type, rounding, saturation);
+  const int in_bytes = type_bytes(from_type), out_bytes = type_bytes(to_type);
+  if (n > 0) {
+    require_ptr(in, "input buffer");
+    require_ptr(out, "output buffer");
+  }
+  if (in % in_bytes != 0 || out % out_bytes != 0)
+    throw std::invalid_argument("Convert buffers must be aligned to their element sizes");
+  constexpr std::uint64_t kElemsPerBlock = 256 * 16;
+  const std::uint64_t blocks = std::max<std::uint64_t>(1, (n + kElemsPerBlock - 1) / kElemsPerBlock);
+  const int grid = static_cast<int>(std::min<std::uint64_t>(blocks, 1u << 20));
+  Current cur(context_);
+  if (cur.result() != CUDA_SUCCESS) return cur.result();
+  ArgumentPack args;
+  args.ptr(in).ptr(out).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32));
+  return cur.finish(launch(function(name), stream, grid, 256, 0, args));
 }
 
 bool Hotpath::has_ordered_kernel(ReduceOp op) { return ordered_kernel_name(op) != nullptr; }

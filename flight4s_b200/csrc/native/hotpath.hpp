@@ -97,6 +97,13 @@ class Hotpath {
   // concatenated in array order).
   CUresult reduce_ordered_final(CUstream stream, CUdeviceptr groups, std::uint64_t count, CUdeviceptr out,
                                 int accumulate);
+  // Elementwise Convert (the reference's Convert node) of n elements from
+  // one launch-ABI type to another: f32 -> f16 / bf16 under a rounding
+  // mode (0 nearest-even, 1 toward zero, 2 toward +inf, 3 toward -inf),
+  // f32 -> FP8 E4M3 / E5M2 under a saturation mode (0 none, 1 finite),
+  // f16 / bf16 / FP8 -> f32, or the same type (a copy).
+  CUresult convert(CUstream stream, int from_type, int to_type, int rounding, int saturation, CUdeviceptr in,
+                   CUdeviceptr out, std::uint64_t n);
   CUresult block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,
                          CUdeviceptr out, CUdeviceptr workspace, std::uint64_t workspace_bytes);
   CUresult vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,

@@ -16,8 +16,8 @@ from typing import Any, Optional
 import numpy as np
 
 from ._native import check, lib
-from .runtime import (BFLOAT16, FLOAT16, FLOAT32, FLOAT64, FP8E4M3, FP8E5M2, INT32, UINT32, CudaContext, CudaModule,
-                      device_address, stream_handle)
+from .runtime import (BFLOAT16, BOOL8, FLOAT16, FLOAT32, FLOAT64, FP8E4M3, FP8E5M2, INT32, UINT32, CudaContext,
+                      CudaModule, device_address, stream_handle)
 
 REDUCE_SUM_F32, REDUCE_SUM_I32, REDUCE_ARGMAX_F32 = 0, 1, 2
 REDUCE_SUM_U32, REDUCE_SUM_F16, REDUCE_SUM_BF16, REDUCE_SUM_F64, REDUCE_SUM_E4M3, REDUCE_SUM_E5M2 = range(3, 9)
@@ -30,6 +30,13 @@ SUM_TYPE_BYTES = {"i32": 4, "u32": 4, "f16": 2, "bf16": 2, "f32": 4, "f64": 8, "
 SUM_HOST_OPS = {"f32": REDUCE_SUM_F32, "i32": REDUCE_SUM_I32, "u32": REDUCE_SUM_U32, "f16": REDUCE_SUM_F16,
                 "bf16": REDUCE_SUM_BF16, "f64": REDUCE_SUM_F64, "e4m3": REDUCE_SUM_E4M3, "e5m2": REDUCE_SUM_E5M2}
 _HOST_OP_BYTES = {REDUCE_ARGMAX_F32: 4, **{op: SUM_TYPE_BYTES[t] for t, op in SUM_HOST_OPS.items()}}
+
+# Convert (core/src/main/scala/flight4s/core/ir/IR.scala:54-70): type codes, RoundingMode and
+# SaturationMode ordinals.  The DSL's FP8 conversions default to SaturateFinite, the rest to NoSaturation.
+CONVERT_TYPE_CODES = {"bool": BOOL8, "i32": INT32, "u32": UINT32, "f16": FLOAT16, "bf16": BFLOAT16, "f32": FLOAT32,
+                      "f64": FLOAT64, "e4m3": FP8E4M3, "e5m2": FP8E5M2}
+ROUNDING = {"nearest_even": 0, "toward_zero": 1, "toward_positive": 2, "toward_negative": 3}
+SATURATION = {"none": 0, "finite": 1}
 
 # ReductionPolicy of the reference's ReduceSum (core/src/main/scala/flight4s/core/ir/IR.scala:79-82)
 POLICIES = {"strict": 0, "deterministic": 1, "fast": 2}
@@ -267,6 +274,23 @@ class Hotpath:
                                                  device_address(ws), _nbytes(ws), stream_handle(copy_stream),
                                                  stream_handle(compute_stream)), "reduce_host_sum_argmax")
         return s, a
+
+    # -------------------------------------------------------------- Convert
+    def convert_into(self, from_dtype: str, to_dtype: str, x: Any, y: Any, n: Optional[int] = None,
+                     rounding: str = "nearest_even", saturation: Optional[str] = None, stream: Any = None) -> None:
+        """y[i] = Convert(x[i]) with the reference's rounding / saturation modes
+        ("nearest_even" | "toward_zero" | "toward_positive" | "toward_negative";
+        "none" | "finite", default "finite" for FP8 targets as in the DSL).
+        Asynchronous."""
+        if saturation is None:
+            saturation = "finite" if to_dtype in ("e4m3", "e5m2") else "none"
+        for d in (from_dtype, to_dtype):
+            if d not in CONVERT_TYPE_CODES:
+                raise ValueError(f"no Convert type {d!r}")
+        check(lib.f4s_convert(self._h, stream_handle(stream), CONVERT_TYPE_CODES[from_dtype],
+                              CONVERT_TYPE_CODES[to_dtype], ROUNDING[rounding], SATURATION[saturation],
+                              device_address(x), device_address(y), _count(x, n)),
+              f"convert {from_dtype} -> {to_dtype}")
 
     # ------------------------------------------------------------ block sum
     @staticmethod

@@ -301,6 +301,25 @@ int f4s_reduce_host_sum_argmax_f32(f4s_hotpath* hotpath, const void* host_in, ui
                                    uint64_t staging_bytes, uint64_t workspace, uint64_t workspace_bytes,
                                    uint64_t copy_stream, uint64_t compute_stream);
 
+/* -------------------------------------------------------------- Convert */
+
+/* The reference's Convert node (core/src/main/scala/flight4s/core/ir/IR.scala:54-70)
+ * over n elements, out[i] = convert(in[i]), types by launch-ABI code:
+ *   6 f32 -> 4 f16 / 5 bf16: rounding 0 NearestEven, 1 TowardZero,
+ *        2 TowardPositive, 3 TowardNegative (__float2half_{rn,rz,ru,rd},
+ *        __float2bfloat16_{rn,rz,ru,rd});
+ *   6 f32 -> 8 e4m3 / 9 e5m2: saturation 0 NoSaturation, 1 SaturateFinite,
+ *        nearest-even whatever `rounding` (__nv_cvt_float_to_fp8);
+ *   4 f16, 5 bf16, 8 e4m3, 9 e5m2 -> 6 f32: exact;
+ *   any type to itself (1..9): a copy.
+ * The codes equal the reference's lowering (CudaCodegen.scala:405-449,506-538)
+ * bit for bit.  Other pairs return F4S_STATUS_INVALID_ARGUMENT with the
+ * reference's message ("cannot emit a conversion from float to double").
+ * Buffers aligned to their element sizes (32-byte alignment of both takes
+ * the vector path).  One launch; asynchronous on `stream`. */
+int f4s_convert(f4s_hotpath* hotpath, uint64_t stream, int32_t from_type, int32_t to_type, int32_t rounding,
+                int32_t saturation, uint64_t in, uint64_t out, uint64_t n);
+
 /* ------------------------------------------------------------ block sum */
 
 /* The reference's blockReduceSum

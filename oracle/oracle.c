@@ -170,6 +170,134 @@ int orc_decode_to_f32(int type_code, const void* x, int64_t n, float* out) {
   return 0;
 }
 
+/* ------------------------------------------------ Convert with modes
+ * The reference's Convert node (core/src/main/scala/flight4s/core/ir/IR.scala:54-70)
+ * carries a RoundingMode {NearestEven, TowardZero, TowardPositive,
+ * TowardNegative} (ordinals 0..3) and a SaturationMode {NoSaturation,
+ * SaturateFinite} (0, 1); its codegen calls __float2half_{rn,rz,ru,rd},
+ * __float2bfloat16_{rn,rz,ru,rd} and __nv_cvt_float_to_fp8(v, sat, kind)
+ * (CudaCodegen.scala:405-449,506-538).  Restated here from IEEE-754 (f16,
+ * bf16) and the OCP FP8 definitions; FP8 conversion always rounds to
+ * nearest-even (the call has no rounding argument). */
+
+/* Round the non-negative quotient m (exact in double) to an integer:
+ * 0 nearest-even, 1 toward zero, 2 away from zero. */
+static double round_magnitude(double m, int mode_on_magnitude) {
+  const double fl = floor(m);
+  switch (mode_on_magnitude) {
+    case 0: return nearbyint(m);           /* default FE_TONEAREST: ties to even */
+    case 1: return fl;
+    default: return fl == m ? m : fl + 1;  /* away from zero */
+  }
+}
+
+/* magnitude rounding for a signed value: RU rounds positive magnitudes up
+ * and negative magnitudes toward zero; RD the reverse */
+static int magnitude_mode(int rounding, int negative) {
+  switch (rounding) {
+    case 0: return 0;
+    case 1: return 1;
+    case 2: return negative ? 1 : 2;
+    default: return negative ? 2 : 1;
+  }
+}
+
+uint16_t orc_f32_to_f16(float f, int rounding) {
+  const uint32_t u = f2u(f);
+  const uint16_t sign = (u >> 31) ? 0x8000 : 0;
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFF;
+  if ((u & 0x7FFFFFFFu) == 0x7F800000u) return sign | 0x7C00;
+  const double a = fabs((double)f);
+  if (a == 0.0) return sign;
+  int k;
+  frexp(a, &k);                  /* a in [2^(k-1), 2^k) */
+  int e = k - 1;
+  if (e < -14) e = -14;          /* subnormal quantum 2^-24 */
+  if (e > 15) e = 15;            /* overflow handled below */
+  const double q = ldexp(1.0, e - 10);
+  const double r = round_magnitude(a / q, magnitude_mode(rounding, sign != 0)) * q;
+  if (r > 65504.0) {
+    const int mm = magnitude_mode(rounding, sign != 0);
+    return sign | (mm == 1 ? 0x7BFF : 0x7C00);   /* toward zero: max finite; else inf */
+  }
+  if (r < 0x1p-14) return sign | (uint16_t)(r / 0x1p-24);
+  int kr;
+  const double fr = frexp(r, &kr);
+  return sign | (uint16_t)(((kr - 1 + 15) << 10) | (uint16_t)((2.0 * fr - 1.0) * 1024.0));
+}
+
+uint16_t orc_f32_to_bf16(float f, int rounding) {
+  if (rounding == 0) return orc_f32_to_bf16_rn(f);
+  const uint32_t u = f2u(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFF;
+  const uint16_t t = (uint16_t)(u >> 16);
+  const int inexact = (u & 0xFFFFu) != 0;
+  const int mm = magnitude_mode(rounding, (u >> 31) != 0);
+  /* magnitude + 1 ulp carries into the exponent (and to inf) by itself */
+  return (mm == 2 && inexact) ? (uint16_t)(t + 1) : t;
+}
+
+uint8_t orc_f32_to_e4m3(float f, int saturate) {
+  if (saturate) return orc_f32_to_e4m3_satfinite(f);
+  const uint8_t sign = (f2u(f) >> 31) ? 0x80 : 0x00;
+  if (isnan(f)) return 0x7F;
+  /* beyond 448 the next step would be 480 = the NaN code: values that round
+   * above 448 (|x| > 464; 464 ties to the even 448) become NaN */
+  if (fabs((double)f) > 464.0) return sign | 0x7F;
+  return orc_f32_to_e4m3_satfinite(f);
+}
+
+/* E5M2: bias 15, 2 mantissa bits, subnormals m * 2^-16, max finite 57344. */
+uint8_t orc_f32_to_e5m2(float f, int saturate) {
+  const uint32_t u = f2u(f);
+  const uint8_t sign = (u >> 31) ? 0x80 : 0x00;
+  if (isnan(f)) return 0x7F;
+  const double a = fabs((double)f);
+  if (isinf(f)) return saturate ? (sign | 0x7B) : (sign | 0x7C);
+  if (a == 0.0) return sign;
+  int k;
+  frexp(a, &k);
+  int e = k - 1;
+  if (e < -14) e = -14;
+  if (e > 15) e = 15;
+  const double q = ldexp(1.0, e - 2);
+  const double r = nearbyint(a / q) * q;
+  if (r > 57344.0) return saturate ? (sign | 0x7B) : (sign | 0x7C);
+  if (r < 0x1p-14) return sign | (uint8_t)(r / 0x1p-16);
+  int kr;
+  const double fr = frexp(r, &kr);
+  return sign | (uint8_t)(((kr - 1 + 15) << 2) | (uint8_t)((2.0 * fr - 1.0) * 4.0));
+}
+
+/* Elementwise Convert over n elements (launch-ABI type codes 4 f16, 5 bf16,
+ * 6 f32, 8 e4m3, 9 e5m2: f32 <-> the others; or any type 1..9 to itself).
+ * Returns 0, or -1 for a pair the reference's codegen rejects. */
+int orc_convert(int from, int to, int rounding, int saturation, const void* in, void* out, int64_t n) {
+  if (from == to) {  /* the reference emits the value unchanged (CudaCodegen.scala:440-441) */
+    static const int kBytes[10] = {0, 1, 4, 4, 2, 2, 4, 8, 1, 1};
+    const int eb = (from >= 1 && from <= 9) ? kBytes[from] : 0;
+    if (eb == 0) return -1;
+    memcpy(out, in, (size_t)(n * eb));
+    return 0;
+  }
+  if (from == 6) {
+    const float* x = (const float*)in;
+    for (int64_t i = 0; i < n; ++i) {
+      switch (to) {
+        case 4: ((uint16_t*)out)[i] = orc_f32_to_f16(x[i], rounding); break;
+        case 5: ((uint16_t*)out)[i] = orc_f32_to_bf16(x[i], rounding); break;
+        case 8: ((uint8_t*)out)[i] = orc_f32_to_e4m3(x[i], saturation); break;
+        case 9: ((uint8_t*)out)[i] = orc_f32_to_e5m2(x[i], saturation); break;
+        default: return -1;
+      }
+    }
+    return 0;
+  }
+  if (to == 6 && (from == 4 || from == 5 || from == 8 || from == 9))
+    return orc_decode_to_f32(from, in, n, (float*)out);
+  return -1;
+}
+
 /* ----------------------------------------------------------- vectorAdd
  * Array.tabulate(n)(i => l(i) + r(i)) (CudaResourcesJniSuite.scala:120-122). */
 void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n) {

@@ -16,6 +16,11 @@ float orc_e4m3_to_f32(uint8_t c);
 float orc_e5m2_to_f32(uint8_t c);
 float orc_f16_to_f32(uint16_t h);
 int orc_decode_to_f32(int type_code, const void* x, int64_t n, float* out);
+uint16_t orc_f32_to_f16(float f, int rounding);
+uint16_t orc_f32_to_bf16(float f, int rounding);
+uint8_t orc_f32_to_e4m3(float f, int saturate);
+uint8_t orc_f32_to_e5m2(float f, int saturate);
+int orc_convert(int from, int to, int rounding, int saturation, const void* in, void* out, int64_t n);
 double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum);
 uint32_t orc_sum_u32(const uint32_t* x, int64_t n);
 double orc_ordered_final(const double* groups, int64_t count);

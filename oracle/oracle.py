@@ -40,6 +40,11 @@ def _load() -> C.CDLL:
         "orc_sum_typed_exactish": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, P(C.c_double)]),
         "orc_sum_u32": (C.c_uint32, [C.c_void_p, C.c_int64]),
         "orc_ordered_final": (C.c_double, [C.c_void_p, C.c_int64]),
+        "orc_f32_to_f16": (C.c_uint16, [C.c_float, C.c_int]),
+        "orc_f32_to_bf16": (C.c_uint16, [C.c_float, C.c_int]),
+        "orc_f32_to_e4m3": (C.c_uint8, [C.c_float, C.c_int]),
+        "orc_f32_to_e5m2": (C.c_uint8, [C.c_float, C.c_int]),
+        "orc_convert": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_sum_ordered": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, P(C.c_int64)]),
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
@@ -181,6 +186,23 @@ def sum_ordered(dtype: str, x: np.ndarray, head: int = 0) -> tuple[float, np.nda
 def ordered_final(groups: np.ndarray) -> float:
     g = np.ascontiguousarray(groups, np.float64)
     return float(lib.orc_ordered_final(_p(g), g.size))
+
+
+CONVERT_STORAGE = {"bool": np.uint8, "i32": np.int32, "u32": np.uint32, "f16": np.uint16, "bf16": np.uint16,
+                   "f32": np.float32, "f64": np.float64, "e4m3": np.uint8, "e5m2": np.uint8}
+CONVERT_CODES = {"bool": 1, **TYPE_CODES}
+
+
+def convert(from_dtype: str, to_dtype: str, x: np.ndarray, rounding: int = 0, saturation: int = 0) -> np.ndarray:
+    """The reference's Convert of each element (raw storage bits for the
+    16-bit and 8-bit float types)."""
+    x = np.ascontiguousarray(x, CONVERT_STORAGE[from_dtype])
+    out = np.empty(x.size, CONVERT_STORAGE[to_dtype])
+    rc = lib.orc_convert(CONVERT_CODES[from_dtype], CONVERT_CODES[to_dtype], rounding, saturation, _p(x), _p(out),
+                         x.size)
+    if rc != 0:
+        raise ValueError(f"cannot convert {from_dtype} -> {to_dtype}")
+    return out
 
 
 def sum_u32(x: np.ndarray) -> int:

@@ -89,6 +89,53 @@ def test_decoder_tables_known_values():
     assert np.array_equal(t["e4m3"], orc.E4M3_TABLE, equal_nan=True)
 
 
+MODED = [("f16", 0), ("f16", 1), ("f16", 2), ("f16", 3), ("bf16", 0), ("bf16", 1), ("bf16", 2), ("bf16", 3),
+         ("e4m3", 0), ("e5m2", 0), ("e5m2", 1)]  # (target, rounding for f16/bf16 | saturation for FP8)
+
+
+def moded_fixture():
+    """Inputs and CUDA's outputs of the Convert node's moded conversions
+    (__float2half_{rn,rz,ru,rd}, __float2bfloat16_{rn,rz,ru,rd},
+    __nv_cvt_float_to_fp8 without / with saturation)."""
+    import lzma
+    raw = lzma.decompress((GOLDEN / "conversions_modes.bin.xz").read_bytes())
+    n = int(np.frombuffer(raw[:4], np.uint32)[0])
+    x = np.frombuffer(raw[4:4 + 4 * n], np.uint32).view(np.float32)
+    outs, off = [], 4 + 4 * n
+    for target, _ in MODED:
+        size = 2 if target in ("f16", "bf16") else 1
+        outs.append(np.frombuffer(raw[off:off + size * n], np.uint16 if size == 2 else np.uint8))
+        off += size * n
+    return x, outs
+
+
+@pytest.mark.parametrize("k", range(len(MODED)))
+def test_moded_conversions_match_cuda_golden(k):
+    target, mode = MODED[k]
+    x, outs = moded_fixture()
+    rounding, saturation = (mode, 0) if target in ("f16", "bf16") else (0, mode)
+    ours = orc.convert("f32", target, x, rounding, saturation)
+    bad = np.nonzero(ours != outs[k])[0]
+    assert bad.size == 0, [(hex(x.view(np.uint32)[i]), hex(ours[i]), hex(outs[k][i])) for i in bad[:8]]
+
+
+def test_exhaustive_moded_check_recorded_zero_mismatches():
+    text = (GOLDEN / "conversions_modes_exhaustive.txt").read_text()
+    assert "fp32 patterns checked: 4294967296" in text
+    lines = [ln for ln in text.splitlines() if "mismatches" in ln]
+    assert len(lines) == 11 and all("mismatches (non-NaN): 0; NaN payload differences: 0" in ln for ln in lines)
+
+
+def test_convert_pairs_and_identity():
+    x = np.array([1.5, -2.25, 65504.0, 1e-8], np.float32)
+    assert np.array_equal(orc.convert("f32", "f32", x), x)
+    assert np.array_equal(orc.convert("f16", "f32", orc.convert("f32", "f16", x)), x[:3].tolist() + [0.0])
+    with pytest.raises(ValueError):
+        orc.convert("f32", "f64", x)
+    with pytest.raises(ValueError):
+        orc.convert("f16", "bf16", np.zeros(2, np.uint16))
+
+
 def test_philox_known_answer_vectors():
     """Random123 Philox4x32-10 known-answer tests."""
     assert orc.philox([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
