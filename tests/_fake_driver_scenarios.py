@@ -192,6 +192,37 @@ def hotpath_dispatch():
     else:
         raise AssertionError("expected ValueError")
     assert count() == before
+    # order-fixed policy: one CTA per 256 KiB group up to the resident CTAs, block 512, no cluster
+    wso = ctx.allocate("u8", hp.policy_workspace_bytes("f32", 1 << 20, "deterministic"))
+    hp.reduce_sum_into("f32", big, out, n=1 << 20, workspace=wso, policy="deterministic")
+    L = check("f4s_reduce_ordered_f32", 16, block=512)
+    assert (param(L, 1, 4), param(L, 5, 4)) == (1 << 20, 0)
+    hp.reduce_sum_into("i32", big, out, n=1 << 20, policy="strict")   # integers: exact under any policy
+    check("f4s_reduce_sum_i32", 16 * 4, block=512, cluster=4)
+    hp.reduce_ordered_final_into(wso.address + 256, 16, out, accumulate=True)
+    L = check("f4s_reduce_ordered_final", 1, block=512)
+    assert (param(L, 1, 4), param(L, 4, 4)) == (16, 1)
+    # Convert: one kernel per pair and mode, grid = one block per 4096 elements
+    for (src, dst, kw, kernel) in [("f32", "f16", {"rounding": "toward_positive"}, "f32_f16_ru"),
+                                   ("f32", "bf16", {"rounding": "toward_negative"}, "f32_bf16_rd"),
+                                   ("f32", "e4m3", {}, "f32_e4m3_sat"),
+                                   ("f32", "e5m2", {"saturation": "none", "rounding": "toward_zero"}, "f32_e5m2_nosat"),
+                                   ("e5m2", "f32", {}, "e5m2_f32"), ("f64", "f64", {}, "copy_8"),
+                                   ("bool", "bool", {}, "copy_1")]:
+        hp.convert_into(src, dst, big, big, n=(1 << 20) + 1, **kw)
+        L = check(f"f4s_convert_{kernel}", 257)
+        assert (param(L, 2, 4), param(L, 3, 4)) == ((1 << 20) + 1, 0)
+    before = count()
+    for (src, dst), msg in [(("f32", "f64"), "cannot emit a conversion from float to double"),
+                            (("f16", "bf16"), "cannot emit a conversion from __half to __nv_bfloat16"),
+                            (("i32", "f32"), "cannot emit a conversion from int to float")]:
+        try:
+            hp.convert_into(src, dst, big, big, n=8)
+        except ValueError as e:
+            assert msg in str(e), (str(e), msg)
+        else:
+            raise AssertionError("expected ValueError")
+    assert count() == before
     parts = ctx.allocate("f32", 4096)
     ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
     hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)

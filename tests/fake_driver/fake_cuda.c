@@ -74,6 +74,15 @@ static const Signature signatures[] = {
     {"f4s_fp8_quant_flat", 4, {8, 8, 8, 4}},
     {"f4s_fp8_quant_rows", 5, {8, 8, 8, 4, 4}},
     {"f4s_fp8_dequant_flat", 4, {8, 8, 8, 4}},
+    {"f4s_convert_f32_f16_ru", 4, {8, 8, 4, 4}},
+    {"f4s_convert_f32_bf16_rd", 4, {8, 8, 4, 4}},
+    {"f4s_convert_f32_e4m3_sat", 4, {8, 8, 4, 4}},
+    {"f4s_convert_f32_e5m2_nosat", 4, {8, 8, 4, 4}},
+    {"f4s_convert_e5m2_f32", 4, {8, 8, 4, 4}},
+    {"f4s_convert_copy_8", 4, {8, 8, 4, 4}},
+    {"f4s_convert_copy_1", 4, {8, 8, 4, 4}},
+    {"f4s_reduce_ordered_f32", 6, {8, 4, 4, 8, 8, 4}},
+    {"f4s_reduce_ordered_final", 5, {8, 4, 4, 8, 4}},
     {"write_values", 2, {8, 4}},
 };
 
