@@ -29,6 +29,7 @@ import json
 import os
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -89,6 +90,36 @@ class ClockSampler:
         except OSError:
             self.proc = None
         self.windows: list[tuple[float, float]] = []
+        # NVML read every ~2 ms as well (nvidia-smi's 100 ms period leaves a
+        # sub-second timed region with one sample or none); read-only queries
+        self.nvml: list[tuple[float, float, float, int]] = []
+        self._handles = []
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            for tok in gpus.split(","):
+                tok = tok.strip()
+                self._handles.append(pynvml.nvmlDeviceGetHandleByIndex(int(tok)) if tok.isdigit()
+                                     else pynvml.nvmlDeviceGetHandleByUUID(tok))
+            self._nv = pynvml
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._handles = []
+
+    def _poll(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            t = time.time()
+            for h in self._handles:
+                try:
+                    self.nvml.append((t, float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                      float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                                      int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                except Exception:
+                    return
+            time.sleep(0.002)
 
     def mark(self, t0: float, t1: float):
         self.windows.append((t0, t1))
@@ -110,6 +141,16 @@ class ClockSampler:
             except ValueError:
                 continue
         self.path.unlink(missing_ok=True)
+        if self._handles:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            nv = self._nv
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            for t, sm, mx, r in self.nvml:
+                rows.append((t, sm, mx, ["Active" if r & b else "Not Active" for b in bits.values()]))
         inside = [r for r in rows if any(a - 0.05 <= r[0] <= b + 0.05 for a, b in self.windows)]
         use = inside or rows
         if not use:
