@@ -78,6 +78,12 @@ class _stdout_to_stderr:
 
 
 # --------------------------------------------------------------- clocks
+def _gpu_uuid(device: int) -> str:
+    """NVML / nvidia-smi identifier of CUDA device `device` of this process."""
+    import torch
+    return "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+
+
 class ClockSampler:
     def __init__(self, gpus: str):
         self.path = Path(f"/tmp/f4s_clocks_{os.getpid()}.csv")
@@ -273,8 +279,8 @@ def main() -> None:
         for _, op in ops:
             op()
     red.wait()
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-    sampler = ClockSampler(visible if visible else ",".join(str(i) for i in range(world))) if rank == 0 else None
+    # the GPUs the ranks use, by UUID (CUDA's device order need not be NVML's)
+    sampler = ClockSampler(",".join(_gpu_uuid(i) for i in range(world))) if rank == 0 else None
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
