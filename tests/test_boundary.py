@@ -186,6 +186,55 @@ def test_native_argument_storage_layout_rules():
     assert list(r.offsets)[:r.count] == [0, 8, 12, 16, 24, 32, 36, 40] and r.size_bytes == 44
 
 
+def test_reference_native_argument_storage_suite_cases():
+    """The known answers of core/src/test/scala/flight4s/core/abi/NativeArgumentStorageSuite.scala."""
+    # "native ABI codes are explicit and unique" (:11-30)
+    codes = [f4s.BOOL8, f4s.INT32, f4s.UINT32, f4s.FLOAT16, f4s.BFLOAT16, f4s.FLOAT32, f4s.FLOAT64, f4s.FP8E4M3,
+             f4s.FP8E5M2, f4s.DEVPTR]
+    assert codes == list(range(1, 11))
+    # "arguments occupy aligned slots in one direct buffer" (:32-67):
+    # (Boolean true, Double 0.0001, Int 37, in[Float] at 0x1122334455667788)
+    s = f4s.NativeArgumentStorage([(f4s.BOOL8, True), (f4s.FLOAT64, 0.0001), (f4s.INT32, 37),
+                                   (f4s.DEVPTR, 0x1122334455667788)])
+    assert list(s.offsets)[:s.count] == [0, 8, 16, 24] and s.size_bytes == 32
+    assert list(s.codes)[:s.count] == [1, 7, 2, 10] and s.address % 8 == 0
+    raw = bytes((C.c_uint8 * 32).from_address(s.address))
+    assert raw[0] == 1 and np.frombuffer(raw[8:16], np.float64)[0] == 0.0001
+    assert int.from_bytes(raw[16:20], "little") == 37
+    assert int.from_bytes(raw[24:32], "little") == 0x1122334455667788
+    # "empty signatures produce empty direct storage" (:69-77)
+    e = f4s.NativeArgumentStorage([])
+    assert e.count == 0 and e.size_bytes == 0
+    # "launch buffer views retain native order" (:79-93): (Int 12, Float 1.5f)
+    v = f4s.NativeArgumentStorage([(f4s.INT32, 12), (f4s.FLOAT32, 1.5)])
+    raw = bytes((C.c_uint8 * 8).from_address(v.address))
+    assert int.from_bytes(raw[0:4], "little") == 12 and np.frombuffer(raw[4:8], np.float32)[0] == 1.5
+
+
+def test_reference_native_launch_request_suite_cases():
+    """The known answers of core/src/test/scala/flight4s/core/abi/NativeLaunchRequestSuite.scala,
+    against the native contract (the Scala-side contract mirrors the C++ one)."""
+    # "flattens geometry and argument metadata" (:17-66): (Int 37, Double 1.25, in[Float])
+    r = f4s.NativeArgumentStorage([(f4s.INT32, 37), (f4s.FLOAT64, 1.25), (f4s.DEVPTR, 0x1122334455667788)])
+    assert list(r.offsets)[:3] == [0, 8, 16] and r.size_bytes == 24 and list(r.codes)[:3] == [2, 7, 10]
+    assert _ours_geometry(18, 4, 2, 32, 8, 1, 2048, 1, 3, 2, 1)[0] == 0
+    # "accepts empty argument storage" (:83-94)
+    buf = (C.c_uint8 * 8)()
+    assert _ours_layout(C.addressof(buf), 0, [], [])[0] == 0
+    # "rejects invalid metadata counts and codes" (:96-113)
+    o = (C.c_int32 * 1)(0)
+    assert _native.lib.f4s_validate_argument_layout(C.addressof(buf), 4, o, 1, None, 0) == -1
+    assert "unknown descriptor code" in _ours_layout(C.addressof(buf), 4, [0], [127])[1]
+    # "rejects invalid offsets and extents" (:115-140)
+    store = (C.c_uint64 * 2)()
+    a = C.addressof(store)
+    assert "negative" in _ours_layout(a, 4, [-1], [2])[1]
+    assert "not aligned to 8 bytes" in _ours_layout(a, 8, [1], [7])[1]
+    assert "overlaps" in _ours_layout(a, 8, [0, 4], [7, 2])[1]
+    for size, offsets, codes in [(4, [0], [7]), (8, [0], [2])]:
+        assert _ours_layout(a, size, offsets, codes)[0] == -1
+
+
 def test_launch_config_validation_messages():
     with pytest.raises(ValueError, match="grid x dimension must be positive"):
         f4s.Grid(0)
