@@ -101,6 +101,7 @@ __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, 
                                                unsigned char* __restrict__ workspace, int accumulate) {
   constexpr int kElem = Op::kElemBytes;
   constexpr int kPerVec = 16 / kElem;
+  static_assert(Op::kUnroll == kReduceUnroll, "order-fixed tiles are 8 vectors per lane");
   __shared__ double tile_partials[2][kGroupTiles];
   __shared__ double scratch[kOrderedWarps];
   __shared__ int is_last;
