@@ -185,7 +185,7 @@ __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, 
            int accumulate) {                                                                              \
     f4s::reduce_ordered<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace, accumulate);                   \
   }
-F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f32, f4s::SumF32Op)
+F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f32, f4s::SumF32TileOp)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_bf16, f4s::SumHalfOp<true>)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f16, f4s::SumHalfOp<false>)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f64, f4s::SumF64Op)

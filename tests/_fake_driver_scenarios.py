@@ -198,7 +198,7 @@ def hotpath_dispatch():
     L = check("f4s_reduce_ordered_f32", 16, block=512)
     assert (param(L, 1, 4), param(L, 5, 4)) == (1 << 20, 0)
     hp.reduce_sum_into("i32", big, out, n=1 << 20, policy="strict")   # integers: exact under any policy
-    check("f4s_reduce_sum_i32", 16 * 4, block=512, cluster=4)
+    check("f4s_reduce_sum_i32", 32 * 4, block=512, cluster=4)
     hp.reduce_ordered_final_into(wso.address + 256, 16, out, accumulate=True)
     L = check("f4s_reduce_ordered_final", 1, block=512)
     assert (param(L, 1, 4), param(L, 4, 4)) == (16, 1)
