@@ -74,14 +74,15 @@ __device__ __forceinline__ double fold_unrolled(float (&s)[U]) {
 // The same tree in f64 over the per-vector f32 sums of the narrow types:
 // an E4M3 vector sum is exact in f32, so E4M3 totals stay exact while they
 // fit f64's 53 bits at the 2^-9 grid (below 2^44, i.e. any n < 2^35).
-__device__ __forceinline__ double fold_unrolled_f64(const float (&s)[kReduceUnroll]) {
-  double d[kReduceUnroll];
+template <int U>
+__device__ __forceinline__ double fold_unrolled_f64(const float (&s)[U]) {
+  double d[U];
 #pragma unroll
-  for (int u = 0; u < kReduceUnroll; ++u) d[u] = static_cast<double>(s[u]);
+  for (int u = 0; u < U; ++u) d[u] = static_cast<double>(s[u]);
 #pragma unroll
-  for (int w = 1; w < kReduceUnroll; w <<= 1) {
+  for (int w = 1; w < U; w <<= 1) {
 #pragma unroll
-    for (int u = 0; u + w < kReduceUnroll; u += 2 * w) d[u] += d[u + w];
+    for (int u = 0; u + w < U; u += 2 * w) d[u] += d[u + w];
   }
   return d[0];
 }
@@ -142,7 +143,7 @@ struct SumHalfOp : SumF64PartialBase {
     for (int u = 0; u < kReduceUnroll; ++u) {
       s[u] = (u < count) ? word(word(0.0f, v[u].x), v[u].y) + word(word(0.0f, v[u].z), v[u].w) : 0.0f;
     }
-    t.acc += fold_unrolled_f64(s);
+    t.acc += fold_unrolled_f64<kReduceUnroll>(s);
   }
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
     const uint32_t w = static_cast<uint32_t>(bits);
@@ -153,10 +154,12 @@ struct SumHalfOp : SumF64PartialBase {
 // FP8 (E4M3 or E5M2) in, f64 out: pairs of codes become f16x2 exactly
 // (cvt.rn.f16x2.{e4m3,e5m2}x2), which the mixed-precision add accumulates in
 // f32 in two chains of eight; every partial sum of E4M3 values is exact in
-// f32 (at most 21 significant bits).  Vector sums are combined in f64.
-template <bool kE4m3>
-struct SumFp8Op : SumF64PartialBase {
+// f32 (at most 21 significant bits).  Vector sums are combined in f64, U per
+// step (the fast kernel 4: +3% at 2 GiB; the order-fixed tiles 8).
+template <bool kE4m3, int U>
+struct SumFp8OpT : SumF64PartialBase {
   static constexpr int kElemBytes = 1;
+  static constexpr int kUnroll = U;
   static __device__ __forceinline__ uint32_t to_f16x2(uint32_t two_codes) {
     if constexpr (kE4m3) return e4m3x2_to_f16x2(two_codes); else return e5m2x2_to_f16x2(two_codes);
   }
@@ -164,33 +167,40 @@ struct SumFp8Op : SumF64PartialBase {
     return add_f16x2_to_f32(add_f16x2_to_f32(acc, to_f16x2(w & 0xFFFFu)), to_f16x2(w >> 16));
   }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
-    float s[kReduceUnroll];
+    float s[U];
 #pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       s[u] = (u < count) ? word(word(0.0f, v[u].x), v[u].y) + word(word(0.0f, v[u].z), v[u].w) : 0.0f;
     }
-    t.acc += fold_unrolled_f64(s);
+    t.acc += fold_unrolled_f64<U>(s);
   }
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t) {
     const uint32_t c = static_cast<uint32_t>(bits) & 0xFFu;
     t.acc += static_cast<double>(kE4m3 ? unpack_e4m3x2(c).x : unpack_e5m2x2(c).x);
   }
 };
+template <bool kE4m3>
+using SumFp8Op = SumFp8OpT<kE4m3, 4>;
+template <bool kE4m3>
+using SumFp8TileOp = SumFp8OpT<kE4m3, kReduceUnroll>;
 
-// f64 in, f64 out.
-struct SumF64Op : SumF64PartialBase {
+// f64 in, f64 out, U vectors per step (the fast kernel 4: +7-9% over 8;
+// the order-fixed tiles 8).
+template <int U>
+struct SumF64OpT : SumF64PartialBase {
   static constexpr int kElemBytes = 8;
+  static constexpr int kUnroll = U;
   static __device__ __forceinline__ double d(uint32_t lo, uint32_t hi) {
     return __hiloint2double(static_cast<int>(hi), static_cast<int>(lo));
   }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t, uint64_t, int count) {
-    double s[kReduceUnroll];
+    double s[U];
 #pragma unroll
-    for (int u = 0; u < kReduceUnroll; ++u) s[u] = (u < count) ? d(v[u].x, v[u].y) + d(v[u].z, v[u].w) : 0.0;
+    for (int u = 0; u < U; ++u) s[u] = (u < count) ? d(v[u].x, v[u].y) + d(v[u].z, v[u].w) : 0.0;
 #pragma unroll
-    for (int w = 1; w < kReduceUnroll; w <<= 1) {
+    for (int w = 1; w < U; w <<= 1) {
 #pragma unroll
-      for (int u = 0; u + w < kReduceUnroll; u += 2 * w) s[u] += s[u + w];
+      for (int u = 0; u + w < U; u += 2 * w) s[u] += s[u + w];
     }
     t.acc += s[0];
   }
@@ -198,6 +208,8 @@ struct SumF64Op : SumF64PartialBase {
     t.acc += __longlong_as_double(static_cast<long long>(bits));
   }
 };
+using SumF64Op = SumF64OpT<4>;
+using SumF64TileOp = SumF64OpT<kReduceUnroll>;
 
 // i32 or u32 in, 32-bit two's-complement wrap out (bit-identical for both).
 struct SumWrap32Op {

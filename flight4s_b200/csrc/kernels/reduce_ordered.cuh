@@ -188,9 +188,9 @@ __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, 
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f32, f4s::SumF32TileOp)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_bf16, f4s::SumHalfOp<true>)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f16, f4s::SumHalfOp<false>)
-F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f64, f4s::SumF64Op)
-F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_e4m3, f4s::SumFp8Op<true>)
-F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_e5m2, f4s::SumFp8Op<false>)
+F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f64, f4s::SumF64TileOp)
+F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_e4m3, f4s::SumFp8TileOp<true>)
+F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_e5m2, f4s::SumFp8TileOp<false>)
 #undef F4S_REDUCE_ORDERED_KERNEL
 
 // F alone over `count` group partials (e.g. several GPUs' partials

@@ -17,7 +17,7 @@ namespace {
 // Launch constants shared with the kernels (csrc/kernels/*.cuh).
 constexpr int kReduceBlock = 512;
 constexpr int kReduceUnroll = 8;
-constexpr int kNarrowStepUnroll = 4;  // vectors per lane per step of the f32 / i32 / argmax kernels (Op::kUnroll)
+constexpr int kShortStepUnroll = 4;
 constexpr int kReduceWaves = 8;
 constexpr std::uint64_t kReducePartialOffset = 256;
 constexpr std::uint64_t kReducePartialBytes = 16;
@@ -290,10 +290,9 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
   // Enough clusters to give each thread >= one unrolled step of 16-byte
   // vectors, at most kReduceWaves waves of co-resident clusters (several
   // waves measured faster than one persistent wave: no idle tail).
-  const int unroll = (op == ReduceOp::kArgmaxF32 || op == ReduceOp::kSumF32 || op == ReduceOp::kSumI32 ||
-                      op == ReduceOp::kSumU32)
-                         ? kNarrowStepUnroll
-                         : kReduceUnroll;
+  // vectors per lane per step of each kernel (its Op::kUnroll): 8 for the
+  // 16-bit sums, 4 for the rest
+  const int unroll = (op == ReduceOp::kSumF16 || op == ReduceOp::kSumBf16) ? kReduceUnroll : kShortStepUnroll;
   const std::uint64_t per_cluster = static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * unroll;
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
   const int clusters = static_cast<int>(

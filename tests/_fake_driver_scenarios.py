@@ -175,10 +175,12 @@ def hotpath_dispatch():
                           ("u32", "i32"), ("i32", "i32"), ("f32", "f32")]:
         hp.reduce_sum_into(dtype, big, out, n=1000)
         check(f"f4s_reduce_sum_{kernel}", 4, block=512, cluster=4)
-    hp.reduce_sum_into("e4m3", big, out, n=1 << 20)  # 4 clusters of 4 x 512 x 16 x 8 elements
-    check("f4s_reduce_sum_e4m3", 4 * 4, block=512, cluster=4)
-    hp.reduce_sum_into("f64", big, out, n=1 << 20)   # 2 elements per vector: 32 clusters
-    check("f4s_reduce_sum_f64", 32 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("e4m3", big, out, n=1 << 20)  # 8 clusters of 4 x 512 x 16 x 4 elements
+    check("f4s_reduce_sum_e4m3", 8 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("bf16", big, out, n=1 << 20)  # 16-bit sums step 8 vectors: 8 clusters of 4 x 512 x 8 x 8
+    check("f4s_reduce_sum_bf16", 8 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("f64", big, out, n=1 << 20)   # 2 elements per vector, 4 per step: 64 clusters
+    check("f4s_reduce_sum_f64", 64 * 4, block=512, cluster=4)
     before = count()
     ws0 = hp.workspace()
     for code in (0, 1, 10, 11):   # bool and pointer have no accumulator
