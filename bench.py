@@ -554,7 +554,10 @@ def profile_run(which: str) -> None:
 
 def kernel_table(ctx, hp, dev, peak) -> dict:
     """The other hot-path kernels at their BASELINE configurations, 1 GPU,
-    CUDA events around `reps` back-to-back launches after warm-up."""
+    CUDA events around `reps` back-to-back launches after warm-up.  Every
+    section allocates its own buffers after releasing the previous ones to
+    the driver: carved out of one reused allocator segment, an input and an
+    output 1 GiB apart measured 3-8% slower for the write-heavy kernels."""
     import torch
 
     import flight4s_b200 as f4s
@@ -596,6 +599,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     hp.fill_synthetic(b, n, f4s.UNIFORM_F32, seed=2)
     row("vector_add_f32 n=2^28", 12 * n, n, timeit(lambda: hp.vector_add_f32(a, b, c, stream=stream)))
     del a, b, c
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
     a = torch.empty(n, dtype=torch.bfloat16, device=dev)
     b = torch.empty_like(a)
     c = torch.empty_like(a)
@@ -603,6 +607,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     hp.fill_synthetic(b, n, f4s.UNIFORM_BF16, seed=2)
     row("vector_add_bf16 n=2^28", 6 * n, n, timeit(lambda: hp.vector_add_bf16(a, b, c, stream=stream)))
     del a, b, c
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
     # block sum, n = 2^20 (4 MiB: L2-resident when hot)
     n = 1 << 20
@@ -640,6 +645,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     flushed = graph_ms(lambda: (flush.zero_(), bs()), 50) - graph_ms(lambda: flush.zero_(), 50)
     row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, flushed, timing="cuda graph")
     del flush
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
     # ReduceSum over the other accumulator input types, 8 GiB of input each
     # (random bits; larger than L2, so no flush is needed between launches)
@@ -657,6 +663,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
             timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream, workspace=ws_o,
                                               policy="deterministic")))
     del raw
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
     # elementwise Convert, 2^28 elements (f32 side 1 GiB)
     n = 1 << 28
@@ -673,6 +680,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     row("convert e4m3->f32 n=2^28", 5 * n, n, timeit(lambda: hp.convert_into("e4m3", "f32", q8, yf, stream=stream)))
     row("convert f16->f32 n=2^28", 6 * n, n, timeit(lambda: hp.convert_into("f16", "f32", h16, yf, stream=stream)))
     del xf, h16, q8, yf
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
     rows, cols = 32768, 8192
     xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)
@@ -685,6 +693,7 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     row("rmsnorm_rows_bf16 32768x8192", 4 * rows * cols + 2 * cols, rows * cols,
         timeit(lambda: hp.rmsnorm_rows_bf16(xb, w, yb, rows, cols, 1e-6, stream=stream)))
     del xb, yb, w
+    torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
     rows = cols = 16384
     n = rows * cols
