@@ -84,6 +84,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "f4s_block_reduce_sum_f32_noalloc": (C.c_int, [vp, u64, u64, i32, u64, u64]),
     "f4s_vector_add_f32": (C.c_int, [vp, u64, u64, u64, u64, i32]),
     "f4s_vector_add_bf16": (C.c_int, [vp, u64, u64, u64, u64, i32]),
+    "f4s_vector_add": (C.c_int, [vp, u64, i32, u64, u64, u64, i32]),
     "f4s_softmax_rows_bf16": (C.c_int, [vp, u64, u64, u64, i32, i32]),
     "f4s_rmsnorm_rows_bf16": (C.c_int, [vp, u64, u64, u64, u64, i32, i32, f32]),
     "f4s_fp8_quantize_e4m3": (C.c_int, [vp, u64, u64, u64, u64, i32, i32]),

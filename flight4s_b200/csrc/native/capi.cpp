@@ -522,6 +522,11 @@ int f4s_vector_add_bf16(f4s_hotpath* hp, uint64_t stream, uint64_t a, uint64_t b
   return guarded([&] { return op_status(hot(hp).vector_add(true, stream_of(stream), a, b, c, n)); });
 }
 
+int f4s_vector_add(f4s_hotpath* hp, uint64_t stream, int32_t type_code, uint64_t a, uint64_t b, uint64_t c,
+                   int32_t n) {
+  return guarded([&] { return op_status(hot(hp).vector_add_typed(type_code, stream_of(stream), a, b, c, n)); });
+}
+
 int f4s_softmax_rows_bf16(f4s_hotpath* hp, uint64_t stream, uint64_t in, uint64_t out, int32_t rows, int32_t cols) {
   return guarded([&] { return op_status(hot(hp).softmax_rows(stream_of(stream), in, out, rows, cols)); });
 }

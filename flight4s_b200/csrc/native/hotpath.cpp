@@ -467,23 +467,38 @@ CUresult Hotpath::block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n,
 
 CUresult Hotpath::vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
                              std::int32_t n) {
+  return vector_add_typed(bf16 ? 5 : 6, stream, a, b, c, n);
+}
+
+CUresult Hotpath::vector_add_typed(int type_code, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
+                                   std::int32_t n) {
+  // AdditiveType (core/src/main/scala/flight4s/core/types/CudaType.scala:154-160)
+  const char* name = nullptr;
+  std::uint64_t elem = 0;
+  switch (type_code) {
+    case 2: case 3: name = "f4s_vector_add_i32"; elem = 4; break;
+    case 4: name = "f4s_vector_add_f16"; elem = 2; break;
+    case 5: name = "f4s_vector_add_bf16"; elem = 2; break;
+    case 6: name = "f4s_vector_add_f32"; elem = 4; break;
+    case 7: name = "f4s_vector_add_f64"; elem = 8; break;
+    default:
+      throw std::invalid_argument("no addition for argument type code " + std::to_string(type_code));
+  }
   require_nonnegative(n, "element count");
   if (n == 0) return CUDA_SUCCESS;
   require_ptr(a, "left buffer");
   require_ptr(b, "right buffer");
   require_ptr(c, "output buffer");
-  const std::uint64_t elem = bf16 ? 2 : 4;
   if (a % elem != 0 || b % elem != 0 || c % elem != 0)
     throw std::invalid_argument("vectorAdd buffers must be aligned to their element size");
   // one thread per 32-byte vector (the kernel loops for any other grid)
-  const std::int64_t per_cta = static_cast<std::int64_t>(kAddBlock) * (bf16 ? 16 : 8);
+  const std::int64_t per_cta = static_cast<std::int64_t>(kAddBlock) * static_cast<std::int64_t>(32 / elem);
   const int grid = static_cast<int>((n + per_cta - 1) / per_cta);
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
   args.ptr(a).ptr(b).ptr(c).i32(n);
-  return cur.finish(launch(function(bf16 ? "f4s_vector_add_bf16" : "f4s_vector_add_f32"), stream,
-                           std::max(grid, 1), kAddBlock, 0, args));
+  return cur.finish(launch(function(name), stream, std::max(grid, 1), kAddBlock, 0, args));
 }
 
 namespace {

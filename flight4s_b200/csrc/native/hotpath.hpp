@@ -106,6 +106,10 @@ class Hotpath {
                    CUdeviceptr out, std::uint64_t n);
   CUresult block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n, CUdeviceptr partials,
                          CUdeviceptr out, CUdeviceptr workspace, std::uint64_t workspace_bytes);
+  // c = a + b for an AdditiveType by launch-ABI code: 2 i32, 3 u32 (32-bit
+  // wrap), 4 f16, 5 bf16 (nearest-even), 6 f32, 7 f64.
+  CUresult vector_add_typed(int type_code, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
+                            std::int32_t n);
   CUresult vector_add(bool bf16, CUstream stream, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c,
                       std::int32_t n);
   CUresult softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out, std::int32_t rows,

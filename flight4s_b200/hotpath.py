@@ -313,6 +313,13 @@ class Hotpath:
         check(lib.f4s_vector_add_bf16(self._h, stream_handle(stream), device_address(a), device_address(b),
                                       device_address(c), _count(a, n)), "vectorAdd bf16")
 
+    def vector_add(self, dtype: str, a: Any, b: Any, c: Any, n: Optional[int] = None, stream: Any = None) -> None:
+        """c = a + b for any AdditiveType: "i32", "u32", "f16", "bf16", "f32", "f64"."""
+        if dtype not in ("i32", "u32", "f16", "bf16", "f32", "f64"):
+            raise ValueError(f"no addition for {dtype!r}")
+        check(lib.f4s_vector_add(self._h, stream_handle(stream), CONVERT_TYPE_CODES[dtype], device_address(a),
+                                 device_address(b), device_address(c), _count(a, n)), f"vectorAdd {dtype}")
+
     # ------------------------------------------------------------- row-wise
     def softmax_rows_bf16(self, x: Any, y: Any, rows: int, cols: int, stream: Any = None) -> None:
         check(lib.f4s_softmax_rows_bf16(self._h, stream_handle(stream), device_address(x), device_address(y),

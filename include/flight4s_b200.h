@@ -355,6 +355,14 @@ int f4s_vector_add_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t left, uin
                        int32_t element_count);
 int f4s_vector_add_bf16(f4s_hotpath* hotpath, uint64_t stream, uint64_t left, uint64_t right, uint64_t output,
                         int32_t element_count);
+/* The same `+` over every AdditiveType of the reference
+ * (core/src/main/scala/flight4s/core/types/CudaType.scala:154-160) by
+ * launch-ABI type code: 2 i32 and 3 u32 (32-bit wrap), 4 f16 and 5 bf16
+ * (IEEE add rounded to nearest-even, the operation of `+` on __half /
+ * __nv_bfloat16), 6 f32, 7 f64.  Other codes return
+ * F4S_STATUS_INVALID_ARGUMENT. */
+int f4s_vector_add(f4s_hotpath* hotpath, uint64_t stream, int32_t type_code, uint64_t left, uint64_t right,
+                   uint64_t output, int32_t element_count);
 
 /* ------------------------------------------------------------ row-wise */
 

@@ -309,6 +309,32 @@ void orc_vector_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int6
   for (int64_t i = 0; i < n; ++i) c[i] = orc_f32_to_bf16_rn(orc_bf16_to_f32(a[i]) + orc_bf16_to_f32(b[i]));
 }
 
+/* `+` over every AdditiveType (CudaType.scala:154-160), by launch-ABI code:
+ * 2/3 32-bit wrap, 4 f16 and 5 bf16 (the f32 sum of the widened operands
+ * rounded to nearest-even once more: f32's 24 bits >= 2 * 11 + 2, so this
+ * equals the correctly rounded 16-bit sum), 6 f32, 7 f64.  -1 otherwise. */
+int orc_vector_add_typed(int type_code, const void* a, const void* b, void* c, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    switch (type_code) {
+      case 2: case 3:
+        ((uint32_t*)c)[i] = ((const uint32_t*)a)[i] + ((const uint32_t*)b)[i];
+        break;
+      case 4:
+        ((uint16_t*)c)[i] = orc_f32_to_f16(orc_f16_to_f32(((const uint16_t*)a)[i]) +
+                                           orc_f16_to_f32(((const uint16_t*)b)[i]), 0);
+        break;
+      case 5:
+        ((uint16_t*)c)[i] = orc_f32_to_bf16_rn(orc_bf16_to_f32(((const uint16_t*)a)[i]) +
+                                               orc_bf16_to_f32(((const uint16_t*)b)[i]));
+        break;
+      case 6: ((float*)c)[i] = ((const float*)a)[i] + ((const float*)b)[i]; break;
+      case 7: ((double*)c)[i] = ((const double*)a)[i] + ((const double*)b)[i]; break;
+      default: return -1;
+    }
+  }
+  return 0;
+}
+
 /* ---------------------------------------------------------- reductions
  * Scala's Array[Float].sum: a left fold in Float from 0.0f
  * (CudaResourcesJniSuite.scala:238). */

@@ -23,6 +23,7 @@ uint8_t orc_f32_to_e5m2(float f, int saturate);
 int orc_convert(int from, int to, int rounding, int saturation, const void* in, void* out, int64_t n);
 double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum);
 uint32_t orc_sum_u32(const uint32_t* x, int64_t n);
+int orc_vector_add_typed(int type_code, const void* a, const void* b, void* c, int64_t n);
 double orc_ordered_final(const double* groups, int64_t count);
 double orc_sum_ordered(int type_code, const void* x, int64_t n, int64_t head, double* groups_out,
                        int64_t* ngroups_out);

@@ -45,6 +45,7 @@ def _load() -> C.CDLL:
         "orc_f32_to_e4m3": (C.c_uint8, [C.c_float, C.c_int]),
         "orc_f32_to_e5m2": (C.c_uint8, [C.c_float, C.c_int]),
         "orc_convert": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int64]),
+        "orc_vector_add_typed": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_sum_ordered": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, P(C.c_int64)]),
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
@@ -203,6 +204,16 @@ def convert(from_dtype: str, to_dtype: str, x: np.ndarray, rounding: int = 0, sa
     if rc != 0:
         raise ValueError(f"cannot convert {from_dtype} -> {to_dtype}")
     return out
+
+
+def vector_add_typed(dtype: str, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """`+` of the reference over any AdditiveType (raw bits for f16 / bf16)."""
+    a = np.ascontiguousarray(a, CONVERT_STORAGE[dtype])
+    b = np.ascontiguousarray(b, CONVERT_STORAGE[dtype])
+    c = np.empty_like(a)
+    if lib.orc_vector_add_typed(CONVERT_CODES[dtype], _p(a), _p(b), _p(c), a.size) != 0:
+        raise ValueError(f"no addition for {dtype}")
+    return c
 
 
 def sum_u32(x: np.ndarray) -> int:

@@ -109,3 +109,59 @@ def test_full_size_2pow28_against_torch(ctx, hp, torch_dev):
                            ref.view(torch.int16) if dtype == torch.bfloat16 else ref.view(torch.int32))
         del a, b, c, ref
     torch.cuda.empty_cache()
+
+
+def _typed_values(dtype, n, seed):
+    rng = np.random.default_rng(seed)
+    if dtype in ("i32", "u32"):
+        return rng.integers(0, 2**32, n, dtype=np.uint64).astype(np.uint32).view(orc.CONVERT_STORAGE[dtype])
+    if dtype == "f16":
+        return (rng.standard_normal(n) * 1000).astype(np.float16).view(np.uint16)
+    if dtype == "bf16":
+        return orc.f32_to_bf16((rng.standard_normal(n) * 1000).astype(np.float32))
+    if dtype == "f32":
+        return (rng.standard_normal(n) * 1000).astype(np.float32)
+    return rng.standard_normal(n) * 1e100
+
+
+@pytest.mark.parametrize("misalign", [0, 1])
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 1000, 65_537, 1_000_003])
+@pytest.mark.parametrize("dtype", ["i32", "u32", "f16", "bf16", "f32", "f64"])
+def test_every_additive_type_bit_exact(ctx, hp, dtype, n, misalign):
+    """f4s_vector_add over the reference's AdditiveTypes, against the
+    oracle's `+` (integers wrap; f16 / bf16 round to nearest-even)."""
+    a, b = _typed_values(dtype, n, n), _typed_values(dtype, n, n + 1)
+    bufs = []
+    for arr in (a, b, np.zeros_like(a)):
+        d = ctx.allocate(dtype, n + misalign)
+        d.copy_from(np.concatenate([np.zeros(misalign, arr.dtype), arr]))
+        bufs.append(d)
+    item = a.itemsize
+    hp.vector_add(dtype, *(d.address + misalign * item for d in bufs), n=n)
+    ctx.synchronize()
+    got = bufs[2].copy_to_array()[misalign:]
+    assert np.array_equal(got.view(np.uint8), orc.vector_add_typed(dtype, a, b).view(np.uint8))
+
+
+def test_f16_special_values(ctx, hp):
+    """Overflow to inf, inf - inf = NaN, subnormal sums, signed zeros."""
+    a = np.array([0x7BFF, 0x7C00, 0x0001, 0x8000, 0x3C00, 0xFC00, 0x03FF], np.uint16)
+    b = np.array([0x7BFF, 0xFC00, 0x0001, 0x0000, 0xBC00, 0xFC00, 0x0001], np.uint16)
+    da, db, dc = (ctx.allocate("f16", a.size) for _ in range(3))
+    da.copy_from(a)
+    db.copy_from(b)
+    hp.vector_add("f16", da, db, dc)
+    ctx.synchronize()
+    got = orc.decode_to_f32("f16", dc.copy_to_array())
+    want = orc.decode_to_f32("f16", orc.vector_add_typed("f16", a, b))
+    assert np.array_equal(got, want, equal_nan=True)
+    assert np.isposinf(got[0]) and np.isnan(got[1]) and np.isneginf(got[5])
+
+
+def test_non_additive_types_are_rejected(ctx, hp):
+    from flight4s_b200 import _native
+    d = ctx.allocate("f32", 8)
+    for code in (1, 8, 9, 10):
+        rc = _native.lib.f4s_vector_add(hp.handle, 0, code, d.address, d.address, d.address, 8)
+        assert rc == _native.STATUS_INVALID_ARGUMENT and "no addition" in _native.last_status()[2]
+
