@@ -145,6 +145,10 @@ def hotpath_dispatch():
     assert param(check("f4s_vector_add_f32", (1 << 28) // 2048), 3, 4) == 1 << 28
     hp.vector_add_bf16(big, big, big, n=1000)
     check("f4s_vector_add_bf16", 1)
+    for dtype, kernel, per_cta in [("f16", "f16", 256 * 16), ("f64", "f64", 256 * 4), ("u32", "i32", 256 * 8)]:
+        hp.vector_add(dtype, big, big, big, n=1 << 20)
+        L = check(f"f4s_vector_add_{kernel}", (1 << 20) // per_cta)
+        assert param(L, 3, 4) == 1 << 20
     hp.softmax_rows_bf16(big, big, 32768, 8192)
     check("f4s_softmax_rows_bf16_v4", 32768)
     hp.softmax_rows_bf16(big, big, 10, 1000)

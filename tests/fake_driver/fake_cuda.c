@@ -62,6 +62,9 @@ typedef struct {
 static const Signature signatures[] = {
     {"f4s_vector_add_f32", 4, {8, 8, 8, 4}},
     {"f4s_vector_add_bf16", 4, {8, 8, 8, 4}},
+    {"f4s_vector_add_f16", 4, {8, 8, 8, 4}},
+    {"f4s_vector_add_f64", 4, {8, 8, 8, 4}},
+    {"f4s_vector_add_i32", 4, {8, 8, 8, 4}},
     {"f4s_reduce_sum_f32", 8, {8, 4, 4, 8, 8, 4, 4, 4}},
     {"f4s_reduce_sum_i32", 8, {8, 4, 4, 8, 8, 4, 4, 4}},
     {"f4s_reduce_argmax_f32", 8, {8, 4, 4, 8, 8, 4, 4, 4}},
