@@ -6,7 +6,7 @@ C ABI that mirrors the reference's native runtime boundary, plus a Python
 mirror of its typed runtime API.  See include/flight4s_b200.h.
 """
 from ._native import CudaDriverFailure, DriverUnavailable, lib  # noqa: F401  (loads the native library)
-from .hotpath import (NORMAL_BF16, NORMAL_BF16_OUTLIERS, NORMAL_F32, REDUCE_ARGMAX_F32, REDUCE_SUM_BF16,  # noqa: F401
+from .hotpath import (ARGMAX_HOST_OPS, argmax_value, NORMAL_BF16, NORMAL_BF16_OUTLIERS, NORMAL_F32, REDUCE_ARGMAX_F32, REDUCE_SUM_BF16,  # noqa: F401
                       REDUCE_SUM_E4M3, REDUCE_SUM_E5M2, REDUCE_SUM_F16, REDUCE_SUM_F32, REDUCE_SUM_F64, REDUCE_SUM_I32,
                       REDUCE_SUM_U32, ROUNDING, SATURATION, CONVERT_TYPE_CODES, SUM_HOST_OPS, SUM_TYPE_CODES, UNIFORM_BF16,
                       UNIFORM_F32, UNIFORM_I32, Hotpath)

@@ -72,6 +72,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "f4s_reduce_sum_i32": (C.c_int, [vp, u64, u64, u64, u64, u64, u64, i32]),
     "f4s_reduce_argmax_f32": (C.c_int, [vp, u64, u64, u64, u64, u64, u64, u64, i32]),
     "f4s_reduce_sum": (C.c_int, [vp, u64, i32, u64, u64, u64, u64, u64, i32]),
+    "f4s_reduce_argmax": (C.c_int, [vp, u64, i32, u64, u64, u64, u64, u64, u64, i32]),
     "f4s_reduce_sum_policy": (C.c_int, [vp, u64, i32, i32, u64, u64, u64, u64, u64, i32]),
     "f4s_reduce_policy_workspace_bytes": (C.c_int, [vp, i32, i32, u64, P(u64)]),
     "f4s_reduce_ordered_groups": (C.c_int, [i32, u64, u64, P(u64)]),

@@ -43,7 +43,7 @@ constexpr int kReducePartialOffset = 256;
 constexpr int kReducePartialBytes = 16;
 
 struct ArgmaxPartial {
-  int32_t key;    // total_order_key of the value
+  int64_t key;    // order key of the value (32-bit keys sign-extended)
   int64_t index;  // INT64_MAX: no candidate
 };
 
@@ -243,25 +243,85 @@ struct SumWrap32Op {
   }
 };
 
-// Output record of the argmax kernel (two 64-bit words):
-//   out[0] = (i64)(order key of the max) << 32 | (0xFFFFFFFF - index): the
-//            packed form whose signed 64-bit max across devices (NCCL
-//            int64 MAX) is again the (max value, lowest index) pair; valid
-//            while index < 2^32; INT64_MIN for an empty input;
+// Order keys: a signed integer whose order is the element type's order
+// (IEEE totalOrder for the floating-point types: -NaN < -inf < ... < -0 <
+// +0 < ... < +inf < +NaN), per OrderedType of the reference
+// (core/src/main/scala/flight4s/core/types/CudaType.scala:182-188).
+struct ArgmaxKeyF32 {
+  static constexpr int kBytes = 4;
+  using Key = int32_t;
+  static __device__ __forceinline__ Key key(uint64_t b) {
+    return total_order_key(__uint_as_float(static_cast<uint32_t>(b)));
+  }
+};
+struct ArgmaxKeyI32 {
+  static constexpr int kBytes = 4;
+  using Key = int32_t;
+  static __device__ __forceinline__ Key key(uint64_t b) { return static_cast<int32_t>(static_cast<uint32_t>(b)); }
+};
+struct ArgmaxKeyU32 {
+  static constexpr int kBytes = 4;
+  using Key = int32_t;
+  static __device__ __forceinline__ Key key(uint64_t b) {
+    return static_cast<int32_t>(static_cast<uint32_t>(b) ^ 0x80000000u);
+  }
+};
+// f16 and bf16 share the sign-magnitude layout, so one key serves both.
+struct ArgmaxKeyHalf {
+  static constexpr int kBytes = 2;
+  using Key = int32_t;
+  static __device__ __forceinline__ Key key(uint64_t b) {
+    const int32_t v = static_cast<int16_t>(static_cast<uint16_t>(b));
+    return v ^ (static_cast<int32_t>(static_cast<uint32_t>(v >> 31) >> 17));
+  }
+};
+struct ArgmaxKeyF64 {
+  static constexpr int kBytes = 8;
+  using Key = int64_t;
+  static __device__ __forceinline__ Key key(uint64_t b) {
+    const int64_t v = static_cast<int64_t>(b);
+    return v ^ static_cast<int64_t>(static_cast<uint64_t>(v >> 63) >> 1);
+  }
+};
+
+// Element j of a 16-byte vector as raw bits.
+template <int kBytes>
+__device__ __forceinline__ uint64_t vector_element(const uint4& v, int j) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (kBytes == 8) return static_cast<uint64_t>(w[2 * j]) | (static_cast<uint64_t>(w[2 * j + 1]) << 32);
+  else if constexpr (kBytes == 4) return w[j];
+  else return (w[j / 2] >> (16 * (j % 2))) & 0xFFFFu;
+}
+
+// Output record of the argmax kernels (two 64-bit words):
+//   out[0] = for 32-bit keys (every type but f64): (i64)key << 32 |
+//            (0xFFFFFFFF - index), the packed form whose signed 64-bit max
+//            across devices (NCCL int64 MAX) is again the (max value, lowest
+//            index) pair, valid while index < 2^32; for f64: the 64-bit key
+//            itself; INT64_MIN for an empty input;
 //   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
-struct ArgmaxF32Op {
-  static constexpr int kElemBytes = 4;
-  // 4 vectors in flight per lane: 39 registers, so 3 CTAs per SM (measured
-  // +5% at 2^29 elements, +2% at 2^32 against 8 vectors at 2 CTAs per SM)
+template <class K>
+struct ArgmaxOp {
+  static constexpr int kElemBytes = K::kBytes;
+  static constexpr int kPerVec = 16 / K::kBytes;
+  // 4 vectors in flight per lane (f32: 39 registers, 3 CTAs per SM; +5% at
+  // 2^29 elements, +2% at 2^32 against 8 vectors at 2 CTAs per SM)
   static constexpr int kUnroll = 4;
+  using Key = typename K::Key;
   using Partial = ArgmaxPartial;
+  static constexpr Key kKeyMin = sizeof(Key) == 8 ? static_cast<Key>(INT64_MIN) : static_cast<Key>(INT32_MIN);
   struct Thread {
-    int32_t vkey = INT32_MIN;  // best key seen in the vector body
+    Key vkey = kKeyMin;  // best key seen in the vector body
     uint64_t best_vec = UINT64_MAX;
     uint4 best = make_uint4(0, 0, 0, 0);  // that vector's values
-    ArgmaxPartial s{INT32_MIN, INT64_MAX};  // scalar head/tail candidate
+    ArgmaxPartial s{INT64_MIN, INT64_MAX};  // scalar head/tail candidate
   };
-  static __device__ __forceinline__ int32_t key(uint32_t b) { return total_order_key(__uint_as_float(b)); }
+  static __device__ __forceinline__ Key vector_max(const uint4& v) {
+    Key k = K::key(vector_element<kElemBytes>(v, 0));
+#pragma unroll
+    for (int j = 1; j < kPerVec; ++j) k = max(k, K::key(vector_element<kElemBytes>(v, j)));
+    return k;
+  }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t base,
                                               uint64_t stride, int count) {
     // The hot loop tracks only the best vector (kept in registers; the
@@ -271,7 +331,7 @@ struct ArgmaxF32Op {
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       if (u < count) {
-        const int32_t k = max(max(key(v[u].x), key(v[u].y)), max(key(v[u].z), key(v[u].w)));
+        const Key k = vector_max(v[u]);
         if (k > t.vkey) {
           t.vkey = k;
           t.best_vec = base + u * stride;
@@ -281,21 +341,21 @@ struct ArgmaxF32Op {
     }
   }
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t index) {
-    argmax_merge(t.s, ArgmaxPartial{key(static_cast<uint32_t>(bits)), static_cast<int64_t>(index)});
+    argmax_merge(t.s, ArgmaxPartial{static_cast<int64_t>(K::key(bits)), static_cast<int64_t>(index)});
   }
   static __device__ __forceinline__ Partial finish(Thread& t, uint64_t head) {
     ArgmaxPartial p = t.s;
     if (t.best_vec != UINT64_MAX) {
-      const uint4 v = t.best;
-      int lane = 3;
-      if (key(v.z) == t.vkey) lane = 2;
-      if (key(v.y) == t.vkey) lane = 1;
-      if (key(v.x) == t.vkey) lane = 0;
-      argmax_merge(p, ArgmaxPartial{t.vkey, static_cast<int64_t>(head + 4 * t.best_vec + lane)});
+      int lane = kPerVec - 1;
+#pragma unroll
+      for (int j = kPerVec - 2; j >= 0; --j)
+        if (K::key(vector_element<kElemBytes>(t.best, j)) == t.vkey) lane = j;
+      argmax_merge(p, ArgmaxPartial{static_cast<int64_t>(t.vkey),
+                                    static_cast<int64_t>(head + kPerVec * t.best_vec + lane)});
     }
     return p;
   }
-  static __device__ __forceinline__ Partial identity() { return ArgmaxPartial{INT32_MIN, INT64_MAX}; }
+  static __device__ __forceinline__ Partial identity() { return ArgmaxPartial{INT64_MIN, INT64_MAX}; }
   static __device__ __forceinline__ Partial merge(Partial a, Partial b) {
     argmax_merge(a, b);
     return a;
@@ -303,32 +363,35 @@ struct ArgmaxF32Op {
   static __device__ __forceinline__ Partial warp_merge(Partial v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      ArgmaxPartial other{__shfl_xor_sync(0xffffffffu, v.key, o),
-                          __shfl_xor_sync(0xffffffffu, v.index, o)};
+      ArgmaxPartial other{__shfl_xor_sync(0xffffffffu, v.key, o), __shfl_xor_sync(0xffffffffu, v.index, o)};
       argmax_merge(v, other);
     }
     return v;
   }
   static __device__ __forceinline__ Partial load_cg(const Partial* p) {
     const longlong2 raw = __ldcg(reinterpret_cast<const longlong2*>(p));
-    return ArgmaxPartial{static_cast<int32_t>(raw.x), static_cast<int64_t>(raw.y)};
+    return ArgmaxPartial{static_cast<int64_t>(raw.x), static_cast<int64_t>(raw.y)};
   }
   static __device__ __forceinline__ void write(void* out, Partial r, uint64_t index_base, int accumulate) {
     int64_t* o = static_cast<int64_t*>(out);
+    constexpr bool kPacked = sizeof(Key) == 4;
     if (r.index != INT64_MAX) r.index += static_cast<int64_t>(index_base);
-    if (accumulate && o[1] >= 0) {
-      argmax_merge(r, ArgmaxPartial{static_cast<int32_t>(o[0] >> 32), o[1]});
-    }
+    if (accumulate && o[1] >= 0) argmax_merge(r, ArgmaxPartial{kPacked ? (o[0] >> 32) : o[0], o[1]});
     if (r.index == INT64_MAX) {
       o[0] = INT64_MIN;
       o[1] = -1;
       return;
     }
-    const uint32_t low = (r.index <= 0xFFFFFFFFll) ? 0xFFFFFFFFu - static_cast<uint32_t>(r.index) : 0u;
-    o[0] = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(r.key)) << 32) | low);
+    if constexpr (kPacked) {
+      const uint32_t low = (r.index <= 0xFFFFFFFFll) ? 0xFFFFFFFFu - static_cast<uint32_t>(r.index) : 0u;
+      o[0] = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(r.key)) << 32) | low);
+    } else {
+      o[0] = r.key;
+    }
     o[1] = r.index;
   }
 };
+using ArgmaxF32Op = ArgmaxOp<ArgmaxKeyF32>;
 
 // Partials are stored as 16-byte records so one workspace layout serves
 // every op.
@@ -485,12 +548,21 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
 // f32 -> f64 sum; i32 / u32 -> 32-bit wrapping sum; f32 max/argmax
 F4S_REDUCE_KERNEL(f4s_reduce_sum_f32, f4s::SumF32Op)
 F4S_REDUCE_KERNEL(f4s_reduce_sum_i32, f4s::SumWrap32Op)
-extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, 3)
-    f4s_reduce_argmax_f32(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace,
-                          uint32_t base_lo, uint32_t base_hi, int accumulate) {
-  f4s::reduce_full<f4s::ArgmaxF32Op>(in, f4s::join_u64(n_lo, n_hi), out, workspace,
-                                     f4s::join_u64(base_lo, base_hi), accumulate);
-}
+// max / argmax over every OrderedType.  MIN_CTAS: 3 per SM where that
+// fits in registers without spilling (f32, 16-bit), else 2.
+#define F4S_ARGMAX_KERNEL(NAME, KEY, MIN_CTAS)                                                         \
+  extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, MIN_CTAS)                             \
+      NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace,           \
+           uint32_t base_lo, uint32_t base_hi, int accumulate) {                                        \
+    f4s::reduce_full<f4s::ArgmaxOp<f4s::KEY>>(in, f4s::join_u64(n_lo, n_hi), out, workspace,            \
+                                              f4s::join_u64(base_lo, base_hi), accumulate);             \
+  }
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f32, ArgmaxKeyF32, 3)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_i32, ArgmaxKeyI32, 2)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_u32, ArgmaxKeyU32, 2)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 3)  // f16 and bf16
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2)
+#undef F4S_ARGMAX_KERNEL
 // the other AccumulatorType inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
 // accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2
 F4S_REDUCE_KERNEL(f4s_reduce_sum_bf16, f4s::SumHalfOp<true>)

@@ -26,6 +26,7 @@ using flight4s::cuda::ReduceOp;
 using flight4s::cuda::kReduceOpCount;
 using flight4s::cuda::ReducePolicy;
 using flight4s::cuda::sum_op_for_type_code;
+using flight4s::cuda::argmax_op_for_type_code;
 
 struct f4s_hotpath {
   Hotpath* impl;
@@ -430,6 +431,14 @@ bool uses_ordered(ReduceOp op, ReducePolicy policy) {
 }
 
 }  // namespace
+
+int f4s_reduce_argmax(f4s_hotpath* hp, uint64_t stream, int32_t input_type, uint64_t in, uint64_t n, uint64_t out,
+                      uint64_t ws, uint64_t ws_bytes, uint64_t index_base, int32_t accumulate) {
+  return guarded([&] {
+    return op_status(hot(hp).reduce(argmax_op_for_type_code(input_type), stream_of(stream), in, n, out, ws, ws_bytes,
+                                    index_base, accumulate));
+  });
+}
 
 int f4s_reduce_sum_policy(f4s_hotpath* hp, uint64_t stream, int32_t input_type, int32_t policy, uint64_t in,
                           uint64_t n, uint64_t out, uint64_t ws, uint64_t ws_bytes, int32_t accumulate) {

@@ -171,6 +171,11 @@ const char* reduce_kernel_name(ReduceOp op) {
     case ReduceOp::kSumF64: return "f4s_reduce_sum_f64";
     case ReduceOp::kSumE4m3: return "f4s_reduce_sum_e4m3";
     case ReduceOp::kSumE5m2: return "f4s_reduce_sum_e5m2";
+    case ReduceOp::kArgmaxI32: return "f4s_reduce_argmax_i32";
+    case ReduceOp::kArgmaxU32: return "f4s_reduce_argmax_u32";
+    case ReduceOp::kArgmaxF16:
+    case ReduceOp::kArgmaxBf16: return "f4s_reduce_argmax_half";  // same 16-bit order key
+    case ReduceOp::kArgmaxF64: return "f4s_reduce_argmax_f64";
   }
   throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
 }
@@ -188,6 +193,11 @@ int reduce_input_bytes(ReduceOp op) {
     case ReduceOp::kSumF64: return 8;
     case ReduceOp::kSumE4m3:
     case ReduceOp::kSumE5m2: return 1;
+    case ReduceOp::kArgmaxI32:
+    case ReduceOp::kArgmaxU32: return 4;
+    case ReduceOp::kArgmaxF16:
+    case ReduceOp::kArgmaxBf16: return 2;
+    case ReduceOp::kArgmaxF64: return 8;
   }
   throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
 }
@@ -196,7 +206,12 @@ int reduce_output_bytes(ReduceOp op) {
   switch (op) {
     case ReduceOp::kSumI32:
     case ReduceOp::kSumU32: return 4;
-    case ReduceOp::kArgmaxF32: return 16;
+    case ReduceOp::kArgmaxF32:
+    case ReduceOp::kArgmaxI32:
+    case ReduceOp::kArgmaxU32:
+    case ReduceOp::kArgmaxF16:
+    case ReduceOp::kArgmaxBf16:
+    case ReduceOp::kArgmaxF64: return 16;
     case ReduceOp::kSumF32:
     case ReduceOp::kSumF16:
     case ReduceOp::kSumBf16:
@@ -205,6 +220,23 @@ int reduce_output_bytes(ReduceOp op) {
     case ReduceOp::kSumE5m2: return 8;  // f64
   }
   throw std::invalid_argument("unknown reduction op " + std::to_string(static_cast<int>(op)));
+}
+
+bool is_argmax(ReduceOp op) {
+  return op == ReduceOp::kArgmaxF32 || static_cast<int>(op) >= static_cast<int>(ReduceOp::kArgmaxI32);
+}
+
+ReduceOp argmax_op_for_type_code(int code) {
+  switch (code) {
+    case 2: return ReduceOp::kArgmaxI32;
+    case 3: return ReduceOp::kArgmaxU32;
+    case 4: return ReduceOp::kArgmaxF16;
+    case 5: return ReduceOp::kArgmaxBf16;
+    case 6: return ReduceOp::kArgmaxF32;
+    case 7: return ReduceOp::kArgmaxF64;
+    default:
+      throw std::invalid_argument("no max/argmax order for argument type code " + std::to_string(code));
+  }
 }
 
 ReduceOp sum_op_for_type_code(int code) {

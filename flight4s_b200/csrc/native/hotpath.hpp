@@ -35,8 +35,14 @@ enum class ReduceOp : int {
   kSumF64 = 6,
   kSumE4m3 = 7,
   kSumE5m2 = 8,
+  // max / argmax over the other OrderedTypes (CudaType.scala:182-188)
+  kArgmaxI32 = 9,
+  kArgmaxU32 = 10,
+  kArgmaxF16 = 11,
+  kArgmaxBf16 = 12,
+  kArgmaxF64 = 13,
 };
-constexpr int kReduceOpCount = 9;
+constexpr int kReduceOpCount = 14;
 
 // Bytes of one input element and of the result record of `op`.
 int reduce_input_bytes(ReduceOp op);
@@ -46,6 +52,10 @@ int reduce_output_bytes(ReduceOp op);
 // 4 f16, 5 bf16, 6 f32, 7 f64, 8 fp8 e4m3, 9 fp8 e5m2); throws
 // std::invalid_argument for codes without an accumulator (bool, pointer).
 ReduceOp sum_op_for_type_code(int code);
+// The max / argmax operator for an OrderedType code (2 i32, 3 u32, 4 f16,
+// 5 bf16, 6 f32, 7 f64); std::invalid_argument otherwise.
+ReduceOp argmax_op_for_type_code(int code);
+bool is_argmax(ReduceOp op);
 
 // The reference's ReductionPolicy (core/src/main/scala/flight4s/core/ir/IR.scala:79-82).
 // Fast: the geometry-sized kernels (reproducible on one device and launch

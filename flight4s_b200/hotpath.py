@@ -29,7 +29,11 @@ SUM_TYPE_BYTES = {"i32": 4, "u32": 4, "f16": 2, "bf16": 2, "f32": 4, "f64": 8, "
 # f4s_reduce_host op of each input type's sum
 SUM_HOST_OPS = {"f32": REDUCE_SUM_F32, "i32": REDUCE_SUM_I32, "u32": REDUCE_SUM_U32, "f16": REDUCE_SUM_F16,
                 "bf16": REDUCE_SUM_BF16, "f64": REDUCE_SUM_F64, "e4m3": REDUCE_SUM_E4M3, "e5m2": REDUCE_SUM_E5M2}
-_HOST_OP_BYTES = {REDUCE_ARGMAX_F32: 4, **{op: SUM_TYPE_BYTES[t] for t, op in SUM_HOST_OPS.items()}}
+# max / argmax over the OrderedTypes: f4s_reduce_host ops and element sizes
+ARGMAX_HOST_OPS = {"f32": REDUCE_ARGMAX_F32, "i32": 9, "u32": 10, "f16": 11, "bf16": 12, "f64": 13}
+ARGMAX_TYPE_BYTES = {"f32": 4, "i32": 4, "u32": 4, "f16": 2, "bf16": 2, "f64": 8}
+_HOST_OP_BYTES = {**{op: SUM_TYPE_BYTES[t] for t, op in SUM_HOST_OPS.items()},
+                  **{op: ARGMAX_TYPE_BYTES[t] for t, op in ARGMAX_HOST_OPS.items()}}
 
 # Convert (core/src/main/scala/flight4s/core/ir/IR.scala:54-70): type codes, RoundingMode and
 # SaturationMode ordinals.  The DSL's FP8 conversions default to SaturateFinite, the rest to NoSaturation.
@@ -64,6 +68,30 @@ def _nbytes(buf: Any) -> int:
     if hasattr(buf, "numel") and hasattr(buf, "element_size"):
         return int(buf.numel() * buf.element_size())
     raise ValueError("buffer size unknown: pass a CudaDeviceBuffer or a torch tensor")
+
+
+def argmax_value(dtype: str, record: np.ndarray) -> tuple[float | int, int]:
+    """(max value, index) of an argmax record of any OrderedType; (nan, -1)
+    when the input was empty."""
+    r = np.ascontiguousarray(record).view(np.int64)
+    index = int(r[1])
+    if index < 0:
+        return float("nan"), -1
+    if dtype == "f64":
+        key = int(r[0])
+        bits = key ^ ((key >> 63) & 0x7FFFFFFFFFFFFFFF)
+        return float(np.array([bits & 0xFFFFFFFFFFFFFFFF], np.uint64).view(np.float64)[0]), index
+    key = int(r[0]) >> 32
+    if dtype == "f32":
+        return unpack_argmax_key(int(r[0]))[0], index
+    if dtype == "i32":
+        return key, index
+    if dtype == "u32":
+        return (key & 0xFFFFFFFF) ^ 0x80000000, index
+    bits = (key ^ ((key >> 31) & 0x7FFF)) & 0xFFFF
+    if dtype == "f16":
+        return float(np.array([bits], np.uint16).view(np.float16)[0]), index
+    return float(np.array([bits << 16], np.uint32).view(np.float32)[0]), index
 
 
 def unpack_argmax_key(packed: int) -> tuple[float, int]:
@@ -195,6 +223,26 @@ class Hotpath:
         if index < 0:
             return float("nan"), -1
         return unpack_argmax_key(int(r[0]))[0], index
+
+    def reduce_argmax_into(self, dtype: str, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
+                           accumulate: bool = False, index_base: int = 0, workspace: Any = None) -> None:
+        """max / argmax over any OrderedType ("i32", "u32", "f16", "bf16",
+        "f32", "f64"): the 16-byte record of f4s_reduce_argmax.  Asynchronous."""
+        if dtype not in ARGMAX_TYPE_BYTES:
+            raise ValueError(f"no max/argmax order for {dtype!r}")
+        ws = self.workspace() if workspace is None else workspace
+        check(lib.f4s_reduce_argmax(self._h, stream_handle(stream), CONVERT_TYPE_CODES[dtype], device_address(x),
+                                    _count(x, n), device_address(out), device_address(ws), _nbytes(ws), index_base,
+                                    int(accumulate)), f"reduce_argmax {dtype}")
+
+    def reduce_argmax(self, dtype: str, x: Any, n: Optional[int] = None, stream: Any = None):
+        """(max value, index of its first occurrence); (nan, -1) when empty."""
+        out = self._result_buffer()
+        self.reduce_argmax_into(dtype, x, out, n=n, stream=stream)
+        if stream is not None and hasattr(stream, "synchronize"):
+            stream.synchronize()
+        self.context.synchronize()
+        return argmax_value(dtype, out.copy_to_array())
 
     def reduce_sum_into(self, dtype: str, x: Any, out: Any, n: Optional[int] = None, stream: Any = None,
                         accumulate: bool = False, workspace: Any = None, policy: str = "fast") -> None:

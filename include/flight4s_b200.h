@@ -232,6 +232,20 @@ int f4s_reduce_argmax_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, ui
                           uint64_t workspace, uint64_t workspace_bytes, uint64_t index_base,
                           int32_t accumulate);
 
+/* max / argmax over every OrderedType of the reference
+ * (core/src/main/scala/flight4s/core/types/CudaType.scala:182-188) by
+ * launch-ABI code: 2 i32, 3 u32, 4 f16, 5 bf16, 6 f32, 7 f64.  Order: the
+ * integers' own; IEEE totalOrder for the floats (-NaN < -inf < ... < -0 <
+ * +0 < ... < +inf < +NaN); ties to the lowest index.  The 16-byte record
+ * is f4s_reduce_argmax_f32's, with the type's order key (i32: the value;
+ * u32: bits ^ 0x80000000; f16 / bf16: bits ^ ((bits >> 15 & 1) * 0x7FFF),
+ * sign-extended; f32: as above) packed in out[0] -- except f64, whose
+ * 64-bit key (bits ^ ((bits >> 63 & 1) * 0x7FFF...F)) fills out[0] alone.
+ * index_base / accumulate as f4s_reduce_argmax_f32. */
+int f4s_reduce_argmax(f4s_hotpath* hotpath, uint64_t stream, int32_t input_type, uint64_t in, uint64_t n,
+                      uint64_t out, uint64_t workspace, uint64_t workspace_bytes, uint64_t index_base,
+                      int32_t accumulate);
+
 /* ReduceSum over every input type the reference accumulates
  * (AccumulatorType, core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
  * selected by its launch-ABI type code
@@ -287,7 +301,9 @@ int f4s_reduce_ordered_final(f4s_hotpath* hotpath, uint64_t stream, uint64_t gro
  * result written to `host_out` (8 / 4 / 16 bytes as above; argmax indices
  * start at `index_base`).  op: 0 sum_f32, 1 sum_i32, 2 argmax_f32,
  * 3 sum_u32, 4 sum_f16, 5 sum_bf16, 6 sum_f64, 7 sum_e4m3, 8 sum_e5m2
- * (results as f4s_reduce_sum).  Synchronizes both streams before returning. */
+ * (results as f4s_reduce_sum), 9 argmax_i32, 10 argmax_u32, 11 argmax_f16,
+ * 12 argmax_bf16, 13 argmax_f64 (records as f4s_reduce_argmax).
+ * Synchronizes both streams before returning. */
 int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint64_t n, uint64_t index_base,
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t workspace,
                     uint64_t workspace_bytes, uint64_t copy_stream, uint64_t compute_stream);

@@ -556,6 +556,38 @@ int64_t orc_argmax_f32(const float* x, int64_t n, float* max_value) {
 
 /* Packed cross-device key, compared as a signed 64-bit integer:
  * (signed totalOrder key << 32) | (0xFFFFFFFF - index). */
+/* max / argmax over every OrderedType (CudaType.scala:182-188) by launch-ABI
+ * code (2 i32, 3 u32, 4 f16, 5 bf16, 6 f32, 7 f64): the first index of the
+ * largest element, integers by value, floats by IEEE totalOrder (the
+ * signed-magnitude bits with the magnitude inverted for negatives); -1 when
+ * n == 0 or the type has no order.  *key_out receives the order key. */
+static int64_t order_key(int type_code, const unsigned char* p) {
+  switch (type_code) {
+    case 2: { int32_t v; memcpy(&v, p, 4); return v; }
+    case 3: { uint32_t v; memcpy(&v, p, 4); return (int64_t)v - 2147483648LL; }
+    case 4: case 5: {
+      int16_t v; memcpy(&v, p, 2);
+      return v < 0 ? (int64_t)(v ^ 0x7FFF) : (int64_t)v;
+    }
+    case 6: { int32_t v; memcpy(&v, p, 4); return v < 0 ? (int64_t)(v ^ 0x7FFFFFFF) : (int64_t)v; }
+    default: { int64_t v; memcpy(&v, p, 8); return v < 0 ? (v ^ INT64_MAX) : v; }
+  }
+}
+
+int64_t orc_argmax_typed(int type_code, const void* x, int64_t n, int64_t* key_out) {
+  static const int kBytes[8] = {0, 0, 4, 4, 2, 2, 4, 8};
+  if (type_code < 2 || type_code > 7 || n <= 0) return -1;
+  const unsigned char* in = (const unsigned char*)x;
+  const int eb = kBytes[type_code];
+  int64_t best = 0, bk = order_key(type_code, in);
+  for (int64_t i = 1; i < n; ++i) {
+    const int64_t k = order_key(type_code, in + i * eb);
+    if (k > bk) { bk = k; best = i; }
+  }
+  if (key_out) *key_out = bk;
+  return best;
+}
+
 int64_t orc_argmax_packed_key(float value, int64_t index) {
   const uint64_t hi = (uint64_t)(uint32_t)total_order_key(value) << 32;
   return (int64_t)(hi | (uint64_t)(0xFFFFFFFFu - (uint32_t)index));

@@ -24,6 +24,7 @@ int orc_convert(int from, int to, int rounding, int saturation, const void* in, 
 double orc_sum_typed_exactish(int type_code, const void* x, int64_t n, double* abs_sum);
 uint32_t orc_sum_u32(const uint32_t* x, int64_t n);
 int orc_vector_add_typed(int type_code, const void* a, const void* b, void* c, int64_t n);
+int64_t orc_argmax_typed(int type_code, const void* x, int64_t n, int64_t* key_out);
 double orc_ordered_final(const double* groups, int64_t count);
 double orc_sum_ordered(int type_code, const void* x, int64_t n, int64_t head, double* groups_out,
                        int64_t* ngroups_out);

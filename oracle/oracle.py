@@ -46,6 +46,7 @@ def _load() -> C.CDLL:
         "orc_f32_to_e5m2": (C.c_uint8, [C.c_float, C.c_int]),
         "orc_convert": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_typed": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
+        "orc_argmax_typed": (C.c_int64, [C.c_int, C.c_void_p, C.c_int64, P(C.c_int64)]),
         "orc_sum_ordered": (C.c_double, [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, P(C.c_int64)]),
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
@@ -214,6 +215,27 @@ def vector_add_typed(dtype: str, a: np.ndarray, b: np.ndarray) -> np.ndarray:
     if lib.orc_vector_add_typed(CONVERT_CODES[dtype], _p(a), _p(b), _p(c), a.size) != 0:
         raise ValueError(f"no addition for {dtype}")
     return c
+
+
+def argmax_typed(dtype: str, x: np.ndarray) -> tuple[int, int]:
+    """(first index of the maximum, its order key) over an OrderedType; (-1, 0) when empty."""
+    x = np.ascontiguousarray(x, CONVERT_STORAGE[dtype])
+    k = C.c_int64()
+    i = lib.orc_argmax_typed(CONVERT_CODES[dtype], _p(x), x.size, C.byref(k))
+    return int(i), int(k.value)
+
+
+def argmax_record(dtype: str, x: np.ndarray, index_base: int = 0) -> list[int]:
+    """The 16-byte record the device writes (two signed 64-bit words)."""
+    i, k = argmax_typed(dtype, x)
+    if i < 0:
+        return [-(1 << 63), -1]
+    i += index_base
+    if dtype == "f64":
+        return [k, i]
+    low = 0xFFFFFFFF - i if i <= 0xFFFFFFFF else 0
+    packed = ((k & 0xFFFFFFFF) << 32) | low
+    return [packed - (1 << 64) if packed >= 1 << 63 else packed, i]
 
 
 def sum_u32(x: np.ndarray) -> int:
