@@ -20,11 +20,12 @@ from __future__ import annotations
 import contextlib
 from typing import Any, Callable, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
-from .hotpath import (ORDERED_GROUP_BYTES, ORDERED_TYPES, POLICIES, REDUCE_ARGMAX_F32, REDUCE_SUM_F32, REDUCE_SUM_I32,
-                      SUM_TYPE_BYTES, SUM_TYPE_CODES, unpack_argmax_key)
+from .hotpath import (ARGMAX_TYPE_BYTES, ORDERED_GROUP_BYTES, ORDERED_TYPES, POLICIES, REDUCE_ARGMAX_F32, REDUCE_SUM_F32,
+                      REDUCE_SUM_I32, SUM_TYPE_BYTES, SUM_TYPE_CODES, argmax_value, unpack_argmax_key)
 
 MAX_PACKED_INDEX = 0xFFFFFFFF  # packed argmax keys carry 32-bit global indices
 
@@ -107,6 +108,7 @@ class ShardedReducer:
         self.arg = torch.zeros(2, dtype=torch.int64, device=device)
         self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
         self.typed: dict[str, torch.Tensor] = {}  # partial of each typed sum
+        self.typed_arg: dict[Any, torch.Tensor] = {}  # record of each typed argmax
         self._ordered: dict[str, dict[str, torch.Tensor]] = {}  # per-type buffers of order-fixed sums
         self._ordered_groups: dict[str, int] = {}  # this rank's group count per type
         self._pending: dict[Any, Any] = {}
@@ -160,6 +162,55 @@ class ShardedReducer:
         self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
         self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
         return self.arg
+
+    def argmax_async(self, dtype: str, shard: torch.Tensor, stream=None) -> torch.Tensor:
+        """max / argmax of any OrderedType over the sharded array.  32-bit
+        order keys travel packed with the index (one all_reduce MAX, as for
+        f32); f64 records are all-gathered and the (max key, lowest index)
+        winner picked on the device.  Returns the combined 16-byte record."""
+        if dtype == "f32":
+            return self.argmax_f32_async(shard, stream)
+        if dtype not in ARGMAX_TYPE_BYTES:
+            raise ValueError(f"no max/argmax order for {dtype!r}")
+        if self.n_total - 1 > MAX_PACKED_INDEX:
+            raise ValueError("sharded argmax packs 32-bit global indices: n_total must be <= 2^32")
+        key = ("argmax", dtype)
+        if key not in self.typed_arg:
+            self.typed_arg[key] = torch.zeros(2, dtype=torch.int64, device=self.device)
+        rec = self.typed_arg[key]
+        self._release(key, shard, stream)
+        s = stream if stream is not None else torch.cuda.current_stream()
+        self.hp.reduce_argmax_into(dtype, shard, rec, n=self.count, stream=s, index_base=self.offset,
+                                   workspace=self.workspace)
+        if self.world == 1:
+            return rec
+        if dtype != "f64":
+            self._combine(key, rec[:1], dist.ReduceOp.MAX, stream)
+            return rec
+        with self._on(stream):
+            gathered = torch.empty(self.world * 2, dtype=torch.int64, device=self.device)
+            dist.all_gather_into_tensor(gathered, rec, group=self.group)
+            g = gathered.view(self.world, 2)
+            valid = g[:, 1] >= 0
+            keys = torch.where(valid, g[:, 0], torch.full_like(g[:, 0], -(1 << 63)))
+            best = keys.max()
+            idx = torch.where(valid & (keys == best), g[:, 1], torch.full_like(g[:, 1], (1 << 63) - 1)).min()
+            rec[0] = torch.where(valid.any(), best, torch.tensor(-(1 << 63), device=self.device))
+            rec[1] = torch.where(valid.any(), idx, torch.tensor(-1, device=self.device))
+        return rec
+
+    def argmax(self, dtype: str, shard: torch.Tensor, stream=None) -> tuple[float | int, int]:
+        rec = self.argmax_async(dtype, shard, stream)
+        self.wait(stream)
+        if dtype == "f32":
+            return self.argmax_result(rec)
+        r = rec.cpu().numpy()
+        if dtype != "f64" and self.world > 1:
+            packed = int(r[0])
+            if packed == -(1 << 63):
+                return float("nan"), -1
+            r = np.array([packed, 0xFFFFFFFF - (packed & 0xFFFFFFFF)], np.int64)
+        return argmax_value(dtype, r)
 
     def _ordered_buffers(self, dtype: str) -> dict[str, torch.Tensor]:
         """Workspace, local / gathered group partials and result of an

@@ -46,6 +46,12 @@ def main() -> None:
         red.sum_async("f16", f16)
         red.wait()
         typed = {k: red.sum(k, v) for k, v in (("u32", xis), ("e4m3", e4m3), ("f16", f16))}
+        f64 = xs.to(torch.float64)
+        for k, v in (("u32", xis.view(torch.int32)), ("f16", f16), ("f64", f64)):
+            red.argmax_async(k, v)
+        red.wait()
+        typed.update({f"argmax_{k}": list(red.argmax(k, v))
+                      for k, v in (("u32", xis.view(torch.int32)), ("f16", f16), ("f64", f64))})
         results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed, "typed": typed})
     # order-fixed sums over granule-aligned shards: the same bits as one GPU
     red_o = ShardedReducer(hp, dev, n_total, granule=ORDERED_GRANULE)

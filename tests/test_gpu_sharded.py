@@ -56,6 +56,10 @@ def test_two_gpu_sharded_reductions_match_oracle(tmp_path, n_total):
         assert t["e4m3"] == orc.sum_typed_exact("e4m3", (xi & 0x7E).astype(np.uint8))[0]  # exact
         h_exact, h_abs = orc.sum_typed_exact("f16", (xi & 0x3BFF).astype(np.uint16))
         assert abs(t["f16"] - h_exact) <= 1e-6 * h_abs
+        for dtype, arr in (("u32", xi.view(np.uint32)), ("f16", (xi & 0x3BFF).astype(np.uint16)),
+                           ("f64", x.astype(np.float64))):
+            i, _ = orc.argmax_typed(dtype, arr)
+            assert t[f"argmax_{dtype}"][1] == i, dtype
     # order-fixed sums: bit-identical to the single-array restatement
     want_f32, _ = orc.sum_ordered("f32", x)
     want_bf16, _ = orc.sum_ordered("bf16", orc.f32_to_bf16(x))
