@@ -3,7 +3,6 @@ bit-exact partials and result vs the oracle's level-by-level tree."""
 import numpy as np
 import pytest
 
-import flight4s_b200 as f4s
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
