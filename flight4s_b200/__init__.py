@@ -9,7 +9,7 @@ from ._native import CudaDriverFailure, DriverUnavailable, lib  # noqa: F401  (l
 from .hotpath import (ARGMAX_HOST_OPS, argmax_value, NORMAL_BF16, NORMAL_BF16_OUTLIERS, NORMAL_F32, REDUCE_ARGMAX_F32, REDUCE_SUM_BF16,  # noqa: F401
                       REDUCE_SUM_E4M3, REDUCE_SUM_E5M2, REDUCE_SUM_F16, REDUCE_SUM_F32, REDUCE_SUM_F64, REDUCE_SUM_I32,
                       REDUCE_SUM_U32, ROUNDING, SATURATION, CONVERT_TYPE_CODES, SUM_HOST_OPS, SUM_TYPE_CODES, UNIFORM_BF16,
-                      UNIFORM_F32, UNIFORM_I32, Hotpath)
+                      UNIFORM_F32, UNIFORM_I32, ORDERED_GROUP_BYTES, ORDERED_TYPES, POLICIES, Hotpath)
 from .runtime import (BFLOAT16, BOOL8, DEVPTR, FLOAT16, FLOAT32, FLOAT64, FP8E4M3, FP8E5M2, INT32, INT64, UINT32,  # noqa: F401
                       Block, Cluster, CudaContext, CudaDeviceBuffer, CudaEvent, CudaFunction, CudaModule,
                       CudaPinnedBuffer, CudaStream, Grid, KernelInvocation, LaunchConfig, NativeArgumentStorage)

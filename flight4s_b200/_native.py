@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "f4s_convert": (C.c_int, [vp, u64, i32, i32, i32, i32, u64, u64, u64]),
     "f4s_reduce_host": (C.c_int, [vp, i32, vp, u64, u64, vp, u64, u64, u64, u64, u64, u64]),
     "f4s_reduce_host_sum_argmax_f32": (C.c_int, [vp, vp, u64, u64, vp, vp, u64, u64, u64, u64, u64, u64]),
+    "f4s_reduce_host_sum_policy": (C.c_int, [vp, i32, i32, vp, u64, vp, u64, u64, u64, u64, u64, u64]),
     "f4s_block_reduce_workspace_bytes": (u64, [i32]),
     "f4s_block_reduce_sum_f32": (C.c_int, [vp, u64, u64, i32, u64, u64, u64, u64]),
     "f4s_block_reduce_sum_f32_noalloc": (C.c_int, [vp, u64, u64, i32, u64, u64]),

@@ -98,7 +98,8 @@ __device__ __forceinline__ double ordered_total(const double* groups, uint64_t c
 
 template <class Op>
 __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, uint64_t n, double* __restrict__ out,
-                                               unsigned char* __restrict__ workspace, int accumulate) {
+                                               unsigned char* __restrict__ workspace, double* __restrict__ groups,
+                                               int accumulate) {
   constexpr int kElem = Op::kElemBytes;
   constexpr int kPerVec = 16 / kElem;
   static_assert(Op::kUnroll == kReduceUnroll, "order-fixed tiles are 8 vectors per lane");
@@ -116,7 +117,6 @@ __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, 
   const uint64_t nvec = nvec_full + (tail > 0 ? 1 : 0);
   const uint64_t ntiles = (nvec + kTileVectors - 1) / kTileVectors;
   const uint64_t ngroups = (ntiles + kGroupTiles - 1) / kGroupTiles;
-  double* groups = reinterpret_cast<double*>(workspace + kOrderedGroupOffset);
   unsigned int* ticket = reinterpret_cast<unsigned int*>(workspace);
 
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -176,14 +176,15 @@ __device__ __forceinline__ void reduce_ordered(const void* __restrict__ in_ptr, 
 
 }  // namespace f4s
 
-// (in, n_lo, n_hi, out f64, workspace, accumulate).  Launch with blockDim
-// 512, any grid; workspace = 256 + 8 * groups bytes, zeroed once (each
-// launch leaves the ticket zeroed; group partials stay readable).
+// (in, n_lo, n_hi, out f64, workspace, groups f64[], accumulate).  Launch
+// with blockDim 512, any grid; workspace holds the ticket (4 bytes, zeroed
+// once; each launch leaves it zeroed), `groups` receives one f64 partial
+// per 256 KiB group (the single-array layout puts it at workspace + 256).
 #define F4S_REDUCE_ORDERED_KERNEL(NAME, OP)                                                              \
   extern "C" __global__ void __launch_bounds__(f4s::kOrderedBlock)                                        \
       NAME(const void* in, uint32_t n_lo, uint32_t n_hi, double* out, unsigned char* workspace,           \
-           int accumulate) {                                                                              \
-    f4s::reduce_ordered<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace, accumulate);                   \
+           double* groups, int accumulate) {                                                              \
+    f4s::reduce_ordered<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace, groups, accumulate);           \
   }
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_f32, f4s::SumF32TileOp)
 F4S_REDUCE_ORDERED_KERNEL(f4s_reduce_ordered_bf16, f4s::SumHalfOp<true>)

@@ -495,6 +495,19 @@ int f4s_reduce_host(f4s_hotpath* hp, int32_t op, const void* host_in, uint64_t n
   });
 }
 
+int f4s_reduce_host_sum_policy(f4s_hotpath* hp, int32_t input_type, int32_t policy, const void* host_in, uint64_t n,
+                               void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t ws,
+                               uint64_t ws_bytes, uint64_t copy_stream, uint64_t compute_stream) {
+  return guarded([&] {
+    const ReduceOp op = sum_op_for_type_code(input_type);
+    if (uses_ordered(op, policy_of(policy)))
+      return op_status(hot(hp).reduce_host_ordered(op, host_in, n, host_out, staging, staging_bytes, ws, ws_bytes,
+                                                   stream_of(copy_stream), stream_of(compute_stream)));
+    return op_status(hot(hp).reduce_host(op, host_in, n, 0, host_out, staging, staging_bytes, ws, ws_bytes,
+                                         stream_of(copy_stream), stream_of(compute_stream)));
+  });
+}
+
 int f4s_reduce_host_sum_argmax_f32(f4s_hotpath* hp, const void* host_in, uint64_t n, uint64_t index_base,
                                    void* host_sum_out, void* host_argmax_out, uint64_t staging,
                                    uint64_t staging_bytes, uint64_t ws, uint64_t ws_bytes, uint64_t copy_stream,

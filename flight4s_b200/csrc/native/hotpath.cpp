@@ -457,7 +457,7 @@ CUresult Hotpath::reduce_ordered(ReduceOp op, CUstream stream, CUdeviceptr in, s
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
   args.ptr(in).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32)).ptr(out).ptr(workspace)
-      .i32(accumulate ? 1 : 0);
+      .ptr(workspace + kOrderedGroupOffset).i32(accumulate ? 1 : 0);
   return cur.finish(launch(function(name), stream, grid, kOrderedBlock, 0, args));
 }
 
@@ -709,27 +709,10 @@ CUresult Hotpath::reduce_host_sum_argmax(const void* host_in, std::uint64_t n, s
                          copy_stream, compute_stream);
 }
 
-CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* host_in, std::uint64_t n,
-                                  std::uint64_t index_base, void* const* host_outs, CUdeviceptr staging,
-                                  std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
-                                  CUstream copy_stream, CUstream compute_stream) {
-  if (n > 0 && host_in == nullptr) throw std::invalid_argument("host input must not be null");
-  for (int i = 0; i < nops; ++i)
-    if (host_outs[i] == nullptr) throw std::invalid_argument("host output must not be null");
-  require_ptr(staging, "staging buffer");
-  if (staging % 256 != 0) throw std::invalid_argument("staging buffer must be 256-byte aligned");
-  if (copy_stream == nullptr || compute_stream == nullptr || copy_stream == compute_stream)
-    throw std::invalid_argument("host-buffer reductions need two distinct non-null streams");
-  // staging = [256 B of device-side results (32 B per op) | buffer 0 | buffer 1]
-  const std::uint64_t half = ((staging_bytes > 256 ? staging_bytes - 256 : 0) / 2) / 256 * 256;
-  if (half < 256) throw std::invalid_argument("staging buffer too small (need >= 768 bytes)");
-  const int elem = reduce_input_bytes(ops[0]);
-  for (int i = 1; i < nops; ++i)
-    if (reduce_input_bytes(ops[i]) != elem) throw std::invalid_argument("fused host reductions need one input type");
-  const std::uint64_t chunk = half / static_cast<std::uint64_t>(elem);  // elements
-  const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
-  auto result_slot = [&](int i) { return staging + 32 * static_cast<CUdeviceptr>(i); };
-
+template <class OnChunk, class OnDone>
+CUresult Hotpath::stream_chunks(const void* host_in, std::uint64_t n, int elem, std::uint64_t chunk,
+                                const CUdeviceptr buffers[2], CUstream copy_stream, CUstream compute_stream,
+                                OnChunk&& on_chunk, OnDone&& on_done) {
   const DriverApi& api = require_driver();
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
@@ -751,15 +734,11 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
                                 copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(copied[b], copy_stream);
     if (r == CUDA_SUCCESS) r = api.cuStreamWaitEvent(compute_stream, copied[b], 0);
-    // every op reduces the same staged chunk (one transfer, nops kernels);
-    // pushing the same context again inside reduce() is harmless
-    for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
-      r = reduce(ops[i], compute_stream, buffers[b], count, result_slot(i), workspace, workspace_bytes,
-                 index_base + first, k > 0 ? 1 : 0);
+    // the ops push the same context again: harmless
+    if (r == CUDA_SUCCESS) r = on_chunk(k, buffers[b], first, count);
     if (r == CUDA_SUCCESS) r = api.cuEventRecord(consumed[b], compute_stream);
   }
-  for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
-    r = api.cuMemcpyDtoHAsync(host_outs[i], result_slot(i), reduce_output_bytes(ops[i]), compute_stream);
+  if (r == CUDA_SUCCESS) r = on_done();
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(compute_stream);
   if (r == CUDA_SUCCESS) r = api.cuStreamSynchronize(copy_stream);
   for (int i = 0; i < 2; ++i) {
@@ -767,6 +746,105 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
     if (consumed[i]) api.cuEventDestroy(consumed[i]);
   }
   return cur.finish(r);
+}
+
+namespace {
+
+// Common checks of the host-buffer entry points; returns the byte size of
+// each staging half (a multiple of 256): staging = [256 B of device-side
+// results (32 B per op) | half 0 | half 1].
+std::uint64_t staging_half(const void* host_in, std::uint64_t n, CUdeviceptr staging, std::uint64_t staging_bytes,
+                           CUstream copy_stream, CUstream compute_stream) {
+  if (n > 0 && host_in == nullptr) throw std::invalid_argument("host input must not be null");
+  require_ptr(staging, "staging buffer");
+  if (staging % 256 != 0) throw std::invalid_argument("staging buffer must be 256-byte aligned");
+  if (copy_stream == nullptr || compute_stream == nullptr || copy_stream == compute_stream)
+    throw std::invalid_argument("host-buffer reductions need two distinct non-null streams");
+  const std::uint64_t half = ((staging_bytes > 256 ? staging_bytes - 256 : 0) / 2) / 256 * 256;
+  if (half < 256) throw std::invalid_argument("staging buffer too small (need >= 768 bytes)");
+  return half;
+}
+
+}  // namespace
+
+CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* host_in, std::uint64_t n,
+                                  std::uint64_t index_base, void* const* host_outs, CUdeviceptr staging,
+                                  std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
+                                  CUstream copy_stream, CUstream compute_stream) {
+  for (int i = 0; i < nops; ++i)
+    if (host_outs[i] == nullptr) throw std::invalid_argument("host output must not be null");
+  const std::uint64_t half = staging_half(host_in, n, staging, staging_bytes, copy_stream, compute_stream);
+  const int elem = reduce_input_bytes(ops[0]);
+  for (int i = 1; i < nops; ++i)
+    if (reduce_input_bytes(ops[i]) != elem) throw std::invalid_argument("fused host reductions need one input type");
+  const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
+  auto result_slot = [&](int i) { return staging + 32 * static_cast<CUdeviceptr>(i); };
+  const DriverApi& api = require_driver();
+  return stream_chunks(
+      host_in, n, elem, half / static_cast<std::uint64_t>(elem), buffers, copy_stream, compute_stream,
+      [&](std::uint64_t k, CUdeviceptr buf, std::uint64_t first, std::uint64_t count) {
+        // every op reduces the same staged chunk (one transfer, nops kernels)
+        CUresult r = CUDA_SUCCESS;
+        for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
+          r = reduce(ops[i], compute_stream, buf, count, result_slot(i), workspace, workspace_bytes,
+                     index_base + first, k > 0 ? 1 : 0);
+        return r;
+      },
+      [&] {
+        CUresult r = CUDA_SUCCESS;
+        for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
+          r = api.cuMemcpyDtoHAsync(host_outs[i], result_slot(i), reduce_output_bytes(ops[i]), compute_stream);
+        return r;
+      });
+}
+
+CUresult Hotpath::reduce_host_ordered(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+                                      CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
+                                      std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream) {
+  const char* name = ordered_kernel_name(op);
+  if (name == nullptr) throw std::invalid_argument("no order-fixed kernel for this reduction");
+  if (host_out == nullptr) throw std::invalid_argument("host output must not be null");
+  const std::uint64_t half = staging_half(host_in, n, staging, staging_bytes, copy_stream, compute_stream);
+  // chunks of whole groups: every chunk starts on a group boundary of the
+  // array, so its group partials are the array's own
+  const std::uint64_t chunk_bytes = half / kOrderedGroupBytes * kOrderedGroupBytes;
+  if (chunk_bytes == 0) {
+    throw std::invalid_argument("staging buffer too small for an order-fixed sum: need >= " +
+                                std::to_string(256 + 2 * kOrderedGroupBytes) + " bytes");
+  }
+  require_ptr(workspace, "reduction workspace");
+  if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
+  const std::uint64_t need = ordered_workspace_bytes(op, n);
+  if (workspace_bytes < need) {
+    throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
+                                " bytes, need " + std::to_string(need));
+  }
+  const std::uint64_t elem = static_cast<std::uint64_t>(reduce_input_bytes(op));
+  const std::uint64_t chunk = chunk_bytes / elem;
+  const std::uint64_t groups_per_chunk = chunk_bytes / kOrderedGroupBytes;
+  const CUdeviceptr buffers[2] = {staging + 256, staging + 256 + half};
+  const CUfunction fn = function(name);
+  const std::uint64_t resident =
+      static_cast<std::uint64_t>(sm_count_) * static_cast<std::uint64_t>(shape_.ordered_ctas_per_sm[static_cast<int>(op)]);
+  const DriverApi& api = require_driver();
+  return stream_chunks(
+      host_in, n, static_cast<int>(elem), chunk, buffers, copy_stream, compute_stream,
+      [&](std::uint64_t k, CUdeviceptr buf, std::uint64_t, std::uint64_t count) {
+        if (count == 0) return CUDA_SUCCESS;
+        const std::uint64_t groups = (count * elem + kOrderedGroupBytes - 1) / kOrderedGroupBytes;
+        const int grid = static_cast<int>(std::max<std::uint64_t>(1, std::min<std::uint64_t>(groups, resident)));
+        // the chunk total lands in the result slot and is overwritten by F
+        ArgumentPack args;
+        args.ptr(buf).u32(static_cast<std::uint32_t>(count)).u32(static_cast<std::uint32_t>(count >> 32))
+            .ptr(staging).ptr(workspace).ptr(workspace + kOrderedGroupOffset + 8 * k * groups_per_chunk).i32(0);
+        return launch(fn, compute_stream, grid, kOrderedBlock, 0, args);
+      },
+      [&] {
+        CUresult r = reduce_ordered_final(compute_stream, workspace + kOrderedGroupOffset, ordered_groups(op, 0, n),
+                                          staging, 0);
+        if (r == CUDA_SUCCESS) r = api.cuMemcpyDtoHAsync(host_out, staging, 8, compute_stream);
+        return r;
+      });
 }
 
 }  // namespace flight4s::cuda

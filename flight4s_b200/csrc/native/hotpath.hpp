@@ -149,6 +149,15 @@ class Hotpath {
                                   std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
                                   CUstream copy_stream, CUstream compute_stream);
 
+  // Order-fixed sum of a HOST buffer: the same pipeline with chunks of
+  // whole 256 KiB groups, each chunk's group partials written to their
+  // place in `workspace` (ordered_workspace_bytes(op, n) bytes), then F over
+  // all of them.  The f64 result is bit-identical to reduce_ordered() of
+  // the same array at a 16-byte-aligned device address.
+  CUresult reduce_host_ordered(ReduceOp op, const void* host_in, std::uint64_t n, void* host_out,
+                               CUdeviceptr staging, std::uint64_t staging_bytes, CUdeviceptr workspace,
+                               std::uint64_t workspace_bytes, CUstream copy_stream, CUstream compute_stream);
+
   // Bounded device-side waits that gave up since the last reset (read after
   // synchronizing the context); non-zero means some output was not written.
   CUresult wait_timeouts(std::uint32_t* count, bool reset);
@@ -168,6 +177,15 @@ class Hotpath {
                            std::uint64_t index_base, void* const* host_outs, CUdeviceptr staging,
                            std::uint64_t staging_bytes, CUdeviceptr workspace, std::uint64_t workspace_bytes,
                            CUstream copy_stream, CUstream compute_stream);
+  // The pipeline itself: chunks of `chunk` elements (> 0) of `elem` bytes
+  // copied into the two halves of the staging area on `copy_stream`;
+  // `on_chunk(k, buffer, first, count)` enqueues chunk k's work on
+  // `compute_stream` (called once with count 0 when n == 0), `on_done()`
+  // the work after the last chunk; then both streams are synchronized.
+  template <class OnChunk, class OnDone>
+  CUresult stream_chunks(const void* host_in, std::uint64_t n, int elem, std::uint64_t chunk,
+                         const CUdeviceptr buffers[2], CUstream copy_stream, CUstream compute_stream,
+                         OnChunk&& on_chunk, OnDone&& on_done);
 
   CUcontext context_ = nullptr;
   CUmodule module_ = nullptr;

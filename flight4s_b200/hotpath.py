@@ -309,6 +309,32 @@ class Hotpath:
                                   stream_handle(copy_stream), stream_handle(compute_stream)), "reduce_host")
         return out
 
+    def reduce_host_sum(self, dtype: str, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
+                        policy: str = "fast", workspace: Any = None) -> float | int:
+        """ReduceSum of a host array (pinned for overlap) under `policy`: the
+        order-fixed policies stage whole 256 KiB groups and give the same
+        bits as `reduce_sum` of the array at a 16-byte-aligned device
+        address, for any staging size."""
+        if dtype not in SUM_TYPE_CODES:
+            raise ValueError(f"no ReduceSum accumulator for {dtype!r}")
+        if policy not in POLICIES:
+            raise ValueError(f"unknown reduction policy {policy!r}")
+        host = np.ascontiguousarray(host)
+        if host.itemsize != SUM_TYPE_BYTES[dtype]:
+            raise ValueError(f"{dtype} sums read {SUM_TYPE_BYTES[dtype]}-byte elements, got {host.dtype}")
+        if workspace is not None:
+            ws = workspace
+        elif policy != "fast" and dtype in ORDERED_TYPES:
+            ws = self.ordered_workspace(self.policy_workspace_bytes(dtype, host.size, policy))
+        else:
+            ws = self.workspace()
+        out = np.zeros(1, np.uint64)
+        check(lib.f4s_reduce_host_sum_policy(self._h, SUM_TYPE_CODES[dtype], POLICIES[policy], host.ctypes.data,
+                                             host.size, out.ctypes.data, device_address(staging), _nbytes(staging),
+                                             device_address(ws), _nbytes(ws), stream_handle(copy_stream),
+                                             stream_handle(compute_stream)), f"reduce_host_sum {dtype} ({policy})")
+        return self.sum_result(dtype, out)
+
     def reduce_host_sum_argmax(self, host: np.ndarray, staging: Any, copy_stream: Any, compute_stream: Any,
                                workspace: Any = None, index_base: int = 0) -> tuple[np.ndarray, np.ndarray]:
         """f32 sum and argmax of a host array from one transfer of each chunk;

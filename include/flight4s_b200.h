@@ -308,6 +308,22 @@ int f4s_reduce_host(f4s_hotpath* hotpath, int32_t op, const void* host_in, uint6
                     void* host_out, uint64_t staging, uint64_t staging_bytes, uint64_t workspace,
                     uint64_t workspace_bytes, uint64_t copy_stream, uint64_t compute_stream);
 
+/* The sum of a HOST buffer of any AdditiveType (input_type as
+ * f4s_reduce_sum) under a ReductionPolicy (as f4s_reduce_sum_policy):
+ * policy 2 Fast (and every integer sum) runs f4s_reduce_host's pipeline;
+ * 0 Strict / 1 Deterministic floating-point sums stage chunks of whole
+ * 256 KiB groups (staging >= 256 + 2 * 262144 bytes) and write each
+ * group's partial to its place in `workspace`
+ * (f4s_reduce_policy_workspace_bytes(n) bytes, ticket zeroed once), then
+ * run F over all of them: the f64 result is bit-identical to
+ * f4s_reduce_sum_policy over the same array at a 16-byte-aligned device
+ * address, whatever the staging size.  Synchronizes both streams before
+ * returning. */
+int f4s_reduce_host_sum_policy(f4s_hotpath* hotpath, int32_t input_type, int32_t policy, const void* host_in,
+                               uint64_t n, void* host_out, uint64_t staging, uint64_t staging_bytes,
+                               uint64_t workspace, uint64_t workspace_bytes, uint64_t copy_stream,
+                               uint64_t compute_stream);
+
 /* The same pipeline computing the f32 sum and the argmax of one host array
  * from a single host->device transfer of each chunk (the two reductions
  * share every staged chunk): host_sum_out receives 8 bytes, host_argmax_out

@@ -202,7 +202,8 @@ def hotpath_dispatch():
     wso = ctx.allocate("u8", hp.policy_workspace_bytes("f32", 1 << 20, "deterministic"))
     hp.reduce_sum_into("f32", big, out, n=1 << 20, workspace=wso, policy="deterministic")
     L = check("f4s_reduce_ordered_f32", 16, block=512)
-    assert (param(L, 1, 4), param(L, 5, 4)) == (1 << 20, 0)
+    assert (param(L, 1, 4), param(L, 6, 4)) == (1 << 20, 0)
+    assert param(L, 5, 8) - param(L, 4, 8) == 256      # group partials follow the 256-byte ticket
     hp.reduce_sum_into("i32", big, out, n=1 << 20, policy="strict")   # integers: exact under any policy
     check("f4s_reduce_sum_i32", 32 * 4, block=512, cluster=4)
     hp.reduce_ordered_final_into(wso.address + 256, 16, out, accumulate=True)
@@ -233,6 +234,68 @@ def hotpath_dispatch():
     ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
     hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)
     check("f4s_block_reduce_sum_f32", 128, block=1024, cluster=8)
+    ctx.close()
+
+
+def host_ordered_pipeline():
+    """Order-fixed sum of a host array: chunks of whole 256 KiB groups, each
+    chunk's partials at its own offset of the group array, then F over all
+    groups; the fast policy keeps the accumulate-per-chunk pipeline."""
+    import numpy as np
+    FAKE.fake_launch_at.restype = C.POINTER(Launch)
+    ctx = f4s.CudaContext.open(0)
+    hp = ctx.hotpath()
+    group = 1 << 18
+    half = 3 * group
+    staging = ctx.allocate("u8", 256 + 2 * half)
+    n = 7 * (group // 4) + 5                    # 8 groups, the last one 20 bytes
+    host = np.zeros(n, np.float32)
+    ws = ctx.allocate("u8", hp.policy_workspace_bytes("f32", n, "deterministic"))
+    assert ws.size_bytes == 256 + 8 * 8
+
+    def launches(since):
+        return [FAKE.fake_launch_at(i).contents for i in range(since, count())]
+
+    before = count()
+    hp.reduce_host_sum("f32", host, staging, 11, 12, policy="deterministic", workspace=ws)
+    L = launches(before)
+    assert [x.name.decode() for x in L] == ["f4s_reduce_ordered_f32"] * 3 + ["f4s_reduce_ordered_final"]
+    for k, (x, elems, grid) in enumerate(zip(L, [3 * group // 4, 3 * group // 4, group // 4 + 5], [3, 3, 2])):
+        assert param(x, 0) == staging.address + 256 + (k % 2) * half
+        assert (param(x, 1, 4), param(x, 2, 4)) == (elems, 0)
+        assert (param(x, 3), param(x, 4)) == (staging.address, ws.address)
+        assert param(x, 5) == ws.address + 256 + 8 * 3 * k and param(x, 6, 4) == 0
+        assert tuple(x.grid) == (grid, 1, 1) and x.block[0] == 512 and x.stream == 12
+    f = L[3]
+    assert (param(f, 0), param(f, 1, 4), param(f, 3), param(f, 4, 4)) == (ws.address + 256, 8, staging.address, 0)
+    # empty input: F over no groups
+    before = count()
+    assert hp.reduce_host_sum("f32", host[:0], staging, 11, 12, policy="strict", workspace=ws) == 0.0
+    assert [x.name.decode() for x in launches(before)] == ["f4s_reduce_ordered_final"]
+    assert param(last(), 1, 4) == 0
+    # fast policy: the geometry-sized kernel per chunk of half / 4 elements, accumulating after the first
+    before = count()
+    hp.reduce_host_sum("f32", host, staging, 11, 12, policy="fast")
+    L = launches(before)
+    assert [x.name.decode() for x in L] == ["f4s_reduce_sum_f32"] * 3
+    assert [param(x, 7, 4) for x in L] == [0, 1, 1]
+    # integers are exact under every policy: the same pipeline
+    before = count()
+    hp.reduce_host_sum("i32", host.view(np.int32), staging, 11, 12, policy="deterministic")
+    assert [x.name.decode() for x in launches(before)] == ["f4s_reduce_sum_i32"] * 3
+    # staging below two groups, a short workspace, one stream twice: rejected before any launch
+    before = count()
+    small = ctx.allocate("u8", 256 + 2 * group - 256)
+    for args, msg in [((small, 11, 12, ws), "too small for an order-fixed sum"),
+                      ((staging, 11, 12, ctx.allocate("u8", 256 + 8 * 7)), "reduction workspace too small"),
+                      ((staging, 11, 11, ws), "two distinct non-null streams")]:
+        try:
+            hp.reduce_host_sum("f32", host, *args[:3], policy="deterministic", workspace=args[3])
+        except ValueError as e:
+            assert msg in str(e), (str(e), msg)
+        else:
+            raise AssertionError("expected ValueError")
+    assert count() == before
     ctx.close()
 
 

@@ -51,6 +51,8 @@ typedef struct {
 
 static Launch last_launch;
 static int launch_count;
+#define HISTORY 64
+static Launch history[HISTORY]; /* launch i (0-based since reset) at history[i % HISTORY] */
 
 typedef struct {
   const char* name;
@@ -84,7 +86,7 @@ static const Signature signatures[] = {
     {"f4s_convert_e5m2_f32", 4, {8, 8, 4, 4}},
     {"f4s_convert_copy_8", 4, {8, 8, 4, 4}},
     {"f4s_convert_copy_1", 4, {8, 8, 4, 4}},
-    {"f4s_reduce_ordered_f32", 6, {8, 4, 4, 8, 8, 4}},
+    {"f4s_reduce_ordered_f32", 7, {8, 4, 4, 8, 8, 8, 4}},
     {"f4s_reduce_ordered_final", 5, {8, 4, 4, 8, 4}},
     {"write_values", 2, {8, 4}},
 };
@@ -96,6 +98,9 @@ typedef struct {
 /* exported for the tests */
 int fake_launch_count(void) { return launch_count; }
 const void* fake_last_launch(void) { return &last_launch; }
+const void* fake_launch_at(int i) {
+  return (i < 0 || i >= launch_count || i + HISTORY < launch_count) ? NULL : &history[i % HISTORY];
+}
 void fake_reset(void) {
   memset(&last_launch, 0, sizeof last_launch);
   launch_count = 0;
@@ -263,6 +268,7 @@ static CUresult f_launch(const CUlaunchConfig* c, CUfunction f, void** params, v
       for (int i = 0; i < signatures[s].n; ++i) memcpy(last_launch.params[i], params[i], signatures[s].sizes[i]);
     }
   }
+  history[launch_count % HISTORY] = last_launch;
   ++launch_count;
   return CUDA_SUCCESS;
 }

@@ -29,6 +29,7 @@ SCENARIOS = {
     "jit_error_log": {"FAKE_CUDA_FAIL": "cuModuleLoadDataEx=218"},
     "invalid_arguments_never_reach_driver": {},
     "hotpath_dispatch": {},
+    "host_ordered_pipeline": {},
 }
 
 

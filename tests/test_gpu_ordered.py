@@ -75,13 +75,15 @@ def test_result_independent_of_grid(ctx, hp, dtype):
     n = (5 << 20) + 11
     x = _values(dtype, n, seed=77)
     buf, addr = _upload(ctx, dtype, x, 0)
-    fn = hp.module.function(f"f4s_reduce_ordered_{dtype}", [DEVPTR, UINT32, UINT32, DEVPTR, DEVPTR, INT32])
+    fn = hp.module.function(f"f4s_reduce_ordered_{dtype}",
+                            [DEVPTR, UINT32, UINT32, DEVPTR, DEVPTR, DEVPTR, INT32])
     ws = ctx.allocate("u8", hp.policy_workspace_bytes(dtype, n, "deterministic"))
     ws.copy_from(np.zeros(ws.element_count, np.uint8))
     out = ctx.allocate("f64", 1)
     want, _ = orc.sum_ordered(dtype, x)
     for grid in (1, 7, 148, 1000):
-        fn.launch(fn.bind(addr, n & 0xFFFFFFFF, n >> 32, out, ws, 0), LaunchConfig(Grid(grid), Block(512)))
+        fn.launch(fn.bind(addr, n & 0xFFFFFFFF, n >> 32, out, ws, ws.address + 256, 0),
+                  LaunchConfig(Grid(grid), Block(512)))
         ctx.synchronize()
         assert _bits(out.copy_to_array()[0]) == _bits(want), grid
 
@@ -111,6 +113,49 @@ def test_group_partials_and_final(ctx, hp, dtype):
     hp.reduce_sum_into(dtype, addr, out, n=n, workspace=ws, policy="strict", accumulate=True)
     ctx.synchronize()
     assert _bits(out.copy_to_array()[0]) == _bits(want + want)
+
+
+HOST_SIZES = [0, 1, 5, 65_536, 65_537, (3 << 18) + 1, (1 << 20) + 7, 3_000_001]
+
+
+@pytest.mark.parametrize("n", HOST_SIZES)
+@pytest.mark.parametrize("dtype", TYPES)
+def test_host_buffer_bit_identical(ctx, hp, dtype, n):
+    """A host array summed through the chunked pipeline gives the bits of
+    the device-resident order-fixed sum at an aligned address, for staging
+    areas of 2, 3 and 5 groups per half (chunk boundaries anywhere)."""
+    x = _values(dtype, n, seed=n + 17)
+    buf, addr = _upload(ctx, dtype, x, 0)
+    want, _ = orc.sum_ordered(dtype, x)
+    assert _bits(hp.reduce_sum(dtype, addr, n=n, policy="deterministic")) == _bits(want)
+    pinned = ctx.allocate_pinned(dtype, max(n, 1))
+    pinned.copy_from(np.concatenate([x, np.zeros(max(n, 1) - n, x.dtype)]))
+    s1, s2 = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    for groups_per_half in (1, 3, 5):
+        staging = ctx.allocate("u8", 256 + 2 * groups_per_half * f4s.ORDERED_GROUP_BYTES + 4096)
+        for policy in ("deterministic", "strict"):
+            got = hp.reduce_host_sum(dtype, pinned.array[:n], staging, s1, s2, policy=policy)
+            assert _bits(got) == _bits(want), (dtype, n, groups_per_half, policy, got, want)
+        staging.close()
+    s1.close()
+    s2.close()
+    buf.close()
+
+
+def test_host_buffer_fast_and_integers(ctx, hp):
+    """The fast policy and the integer sums keep the per-chunk pipeline."""
+    x = _values("f32", 1_000_003, seed=4)
+    xi = np.random.default_rng(2).integers(-2**31, 2**31, 1_000_003, dtype=np.int64).astype(np.int32)
+    staging = ctx.allocate("u8", 256 + 2 * 65536)
+    s1, s2 = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    exact, abs_sum = orc.sum_f32_exact(x)
+    assert abs(hp.reduce_host_sum("f32", x, staging, s1, s2) - exact) <= 1e-6 * abs_sum
+    for policy in ("strict", "fast"):
+        assert hp.reduce_host_sum("i32", xi, staging, s1, s2, policy=policy) == orc.sum_i32(xi)
+    with pytest.raises(ValueError, match="too small for an order-fixed sum"):
+        hp.reduce_host_sum("f32", x, staging, s1, s2, policy="deterministic")
+    s1.close()
+    s2.close()
 
 
 def test_workspace_checks(ctx, hp):
