@@ -100,7 +100,6 @@ Hotpath* Hotpath::open(CUcontext context) {
       return std::max(1, blocks);
     };
     hp->shape_.add_grid = hp->sm_count_ * occupancy("f4s_vector_add_f32", kAddBlock);
-    hp->shape_.row_ctas_per_sm = occupancy("f4s_softmax_rows_bf16_v4", kRowBlock);
     hp->shape_.fp8_grid = hp->sm_count_ * occupancy("f4s_fp8_quant_flat", kFp8Threads);
     hp->shape_.fill_grid = hp->sm_count_ * occupancy("f4s_fill_synthetic", 256);
     for (int op = 0; op < kReduceOpCount; ++op) {
@@ -558,14 +557,7 @@ CUresult Hotpath::softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out,
   const int vpt = row_vectors_per_thread(cols, in, out);
   const std::string name = vpt ? "f4s_softmax_rows_bf16_v" + std::to_string(vpt) : "f4s_softmax_rows_bf16_any";
   const CUfunction fn = function(name);
-  int per_sm = shape_.row_ctas_per_sm;
-  {
-    int blocks = 0;
-    if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
-      per_sm = blocks;
-  }
   // one CTA per row (measured best: no persistent tail)
-  (void)per_sm;
   const int grid = rows;
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
@@ -599,15 +591,8 @@ CUresult Hotpath::rmsnorm_rows(CUstream stream, CUdeviceptr in, CUdeviceptr weig
   }
   const std::string name = vpt ? "f4s_rmsnorm_rows_bf16_v" + std::to_string(vpt) : "f4s_rmsnorm_rows_bf16_any";
   const CUfunction fn = function(name);
-  int per_sm = shape_.row_ctas_per_sm;
-  {
-    int blocks = 0;
-    if (require_driver().cuOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kRowBlock, 0) == CUDA_SUCCESS && blocks > 0)
-      per_sm = blocks;
-  }
   // Persistent CTAs (8 per SM, measured flat between 2 and 8 for 8192-wide
   // rows), each keeping its weight slice in registers across its rows.
-  (void)per_sm;
   const int grid = static_cast<int>(std::min<std::int64_t>(rows, static_cast<std::int64_t>(sm_count_) * 8));
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();

@@ -69,7 +69,6 @@ struct HotpathShape {
   int reduce_cluster = 4;       // CTAs per cluster in the full-array reductions
   int reduce_max_clusters[kReduceOpCount] = {};  // co-resident clusters per op (occupancy query)
   int add_grid = 0;
-  int row_ctas_per_sm = 0;
   int fp8_grid = 0;
   int fill_grid = 0;
   int ordered_ctas_per_sm[kReduceOpCount] = {};  // order-fixed sums (float ops only)
