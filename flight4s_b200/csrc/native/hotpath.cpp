@@ -282,6 +282,36 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
   return scope.close();
 }
 
+namespace {
+
+// 16-byte vectors per lane per step of each fast kernel (its Op::kUnroll in
+// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums, 4 for the rest.
+int reduce_step_vectors(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumF16:
+    case ReduceOp::kSumBf16:
+    case ReduceOp::kSumF64:
+    case ReduceOp::kSumE4m3:
+    case ReduceOp::kSumE5m2: return kReduceUnroll;
+    default: return kShortStepUnroll;
+  }
+}
+
+// Waves of co-resident clusters in one launch: kReduceWaves, doubled for the
+// f64 and FP8 sums, whose kernels hold two CTAs per SM (~4544 CTAs either
+// way; measured +2-6 % over 8 waves at 2 and 8 GiB).  Every choice stays
+// within reduce_workspace_bytes(): at most 4 CTAs per SM x kReduceWaves.
+int reduce_waves(ReduceOp op) {
+  switch (op) {
+    case ReduceOp::kSumF64:
+    case ReduceOp::kSumE4m3:
+    case ReduceOp::kSumE5m2: return 2 * kReduceWaves;
+    default: return kReduceWaves;
+  }
+}
+
+}  // namespace
+
 std::uint64_t Hotpath::reduce_workspace_bytes() const {
   // One partial slot per launched cluster; kReduceWaves waves of at most
   // 2048 / kReduceBlock co-resident CTAs per SM bound every cluster size.
@@ -321,14 +351,12 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
   // Enough clusters to give each thread >= one unrolled step of 16-byte
   // vectors, at most kReduceWaves waves of co-resident clusters (several
   // waves measured faster than one persistent wave: no idle tail).
-  // vectors per lane per step of each kernel (its Op::kUnroll): 8 for the
-  // 16-bit sums, 4 for the rest
-  const int unroll = (op == ReduceOp::kSumF16 || op == ReduceOp::kSumBf16) ? kReduceUnroll : kShortStepUnroll;
-  const std::uint64_t per_cluster = static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * unroll;
+  const std::uint64_t per_cluster =
+      static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * reduce_step_vectors(op);
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
   const int clusters = static_cast<int>(
       std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters[static_cast<int>(op)]) *
-                                          kReduceWaves));
+                                          reduce_waves(op)));
   const std::uint64_t need = kReducePartialOffset + kReducePartialBytes * static_cast<std::uint64_t>(clusters);
   if (workspace_bytes < need) {
     throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +

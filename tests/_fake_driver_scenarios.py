@@ -179,12 +179,20 @@ def hotpath_dispatch():
                           ("u32", "i32"), ("i32", "i32"), ("f32", "f32")]:
         hp.reduce_sum_into(dtype, big, out, n=1000)
         check(f"f4s_reduce_sum_{kernel}", 4, block=512, cluster=4)
-    hp.reduce_sum_into("e4m3", big, out, n=1 << 20)  # 8 clusters of 4 x 512 x 16 x 4 elements
-    check("f4s_reduce_sum_e4m3", 8 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("e4m3", big, out, n=1 << 20)  # FP8 steps 8 vectors: 4 clusters of 4 x 512 x 16 x 8 elements
+    check("f4s_reduce_sum_e4m3", 4 * 4, block=512, cluster=4)
     hp.reduce_sum_into("bf16", big, out, n=1 << 20)  # 16-bit sums step 8 vectors: 8 clusters of 4 x 512 x 8 x 8
     check("f4s_reduce_sum_bf16", 8 * 4, block=512, cluster=4)
-    hp.reduce_sum_into("f64", big, out, n=1 << 20)   # 2 elements per vector, 4 per step: 64 clusters
-    check("f4s_reduce_sum_f64", 64 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("f64", big, out, n=1 << 20)   # 2 elements per vector, 8 per step: 32 clusters
+    check("f4s_reduce_sum_f64", 32 * 4, block=512, cluster=4)
+    # large inputs: 8 waves of co-resident clusters (the fake reports 37), 16 for the f64 and FP8 sums
+    hp.reduce_sum_into("f64", big, out, n=1 << 27)
+    check("f4s_reduce_sum_f64", 37 * 16 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("e5m2", big, out, n=1 << 30)
+    check("f4s_reduce_sum_e5m2", 37 * 16 * 4, block=512, cluster=4)
+    hp.reduce_sum_into("f16", big, out, n=1 << 29)
+    check("f4s_reduce_sum_f16", 37 * 8 * 4, block=512, cluster=4)
+    assert 256 + 16 * (37 * 16) <= hp.workspace_bytes   # one 16-byte partial slot per launched cluster
     before = count()
     ws0 = hp.workspace()
     for code in (0, 1, 10, 11):   # bool and pointer have no accumulator
