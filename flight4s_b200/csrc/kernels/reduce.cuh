@@ -275,6 +275,19 @@ struct ArgmaxKeyHalf {
     const int32_t v = static_cast<int16_t>(static_cast<uint16_t>(b));
     return v ^ (static_cast<int32_t>(static_cast<uint32_t>(v >> 31) >> 17));
   }
+  // The same keys two at a time: each 16-bit lane of `w` XOR 0x7FFF where
+  // its sign bit is set ((sign bits >> 15) * 0x7FFF stays inside each lane).
+  static __device__ __forceinline__ uint32_t keys2(uint32_t w) { return w ^ (((w >> 15) & 0x00010001u) * 0x7FFFu); }
+  static __device__ __forceinline__ uint32_t max_s16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  // max key of a 16-byte vector (8 elements), as key() would give it.
+  static __device__ __forceinline__ Key vector_max(const uint4& v) {
+    const uint32_t m = max_s16x2(max_s16x2(keys2(v.x), keys2(v.y)), max_s16x2(keys2(v.z), keys2(v.w)));
+    return max(static_cast<int32_t>(static_cast<int16_t>(m & 0xFFFFu)), static_cast<int32_t>(m) >> 16);
+  }
 };
 struct ArgmaxKeyF64 {
   static constexpr int kBytes = 8;
@@ -318,10 +331,14 @@ struct ArgmaxOp {
     ArgmaxPartial s{INT64_MIN, INT64_MAX};  // scalar head/tail candidate
   };
   static __device__ __forceinline__ Key vector_max(const uint4& v) {
-    Key k = K::key(vector_element<kElemBytes>(v, 0));
+    if constexpr (kElemBytes == 2) {
+      return K::vector_max(v);  // packed 16-bit keys
+    } else {
+      Key k = K::key(vector_element<kElemBytes>(v, 0));
 #pragma unroll
-    for (int j = 1; j < kPerVec; ++j) k = max(k, K::key(vector_element<kElemBytes>(v, j)));
-    return k;
+      for (int j = 1; j < kPerVec; ++j) k = max(k, K::key(vector_element<kElemBytes>(v, j)));
+      return k;
+    }
   }
   static __device__ __forceinline__ void body(Thread& t, const uint4* v, uint64_t base,
                                               uint64_t stride, int count) {
