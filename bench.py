@@ -487,6 +487,13 @@ def profile_run(which: str) -> None:
         for k in typed:
             rep(lambda: hp.reduce_sum_into(k, raw, out, n=(1 << 30) // f4s.hotpath.SUM_TYPE_BYTES[k]))
         del raw
+    typed_arg = [k for k in ("f16", "i32", "u32", "f64") if want(f"reduce_argmax_{k}")]
+    if typed_arg:
+        raw = torch.randint(0, 256, (1 << 30,), dtype=torch.uint8, device=dev)
+        out = torch.zeros(2, dtype=torch.int64, device=dev)
+        for k in typed_arg:
+            rep(lambda: hp.reduce_argmax_into(k, raw, out, n=(1 << 30) // f4s.hotpath.ARGMAX_TYPE_BYTES[k]))
+        del raw
     if want("reduce_ordered_f32"):
         raw = torch.randint(0, 256, (1 << 30,), dtype=torch.uint8, device=dev)
         out = torch.zeros(2, dtype=torch.int64, device=dev)
@@ -655,6 +662,11 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
         count = (8 << 30) // size
         row(f"reduce_sum_{dtype} 8 GiB", 8 << 30, count,
             timeit(lambda: hp.reduce_sum_into(dtype, raw, acc, n=count, stream=stream)))
+    # max / argmax over the other OrderedTypes (16-byte records), same bytes
+    for dtype, size in [("f16", 2), ("i32", 4), ("u32", 4), ("f64", 8)]:
+        count = (8 << 30) // size
+        row(f"reduce_argmax_{dtype} 8 GiB", 8 << 30, count,
+            timeit(lambda: hp.reduce_argmax_into(dtype, raw, acc, n=count, stream=stream)))
     # the order-fixed ("deterministic") policy of the same sums
     for dtype, size in [("f32", 4), ("bf16", 2), ("e4m3", 1)]:
         count = (8 << 30) // size
