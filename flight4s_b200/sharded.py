@@ -83,6 +83,40 @@ def combine_argmax(packed: torch.Tensor, group: Any = None) -> torch.Tensor:
     return packed
 
 
+_I64_MIN, _I64_MAX = -(1 << 63), (1 << 63) - 1
+
+
+def combine_argmax_records(rec: torch.Tensor, key_bits: int, group: Any = None) -> torch.Tensor:
+    """Replace this rank's argmax record `rec` = [word0, index] (int64[2],
+    index -1 when the shard was empty) by the global one: the records are
+    all-gathered and every rank picks the largest order key, lowest global
+    index on ties.  word0 is the key itself for 64-bit keys (f64) and the
+    packed form (key << 32 | 0xFFFFFFFF - index) for 32-bit keys; the
+    result keeps that form (low word 0 when the index needs more than 32
+    bits) and carries the full index in rec[1].  For 64-bit keys, and for
+    arrays whose indices exceed the 32 bits a packed key can carry."""
+    if key_bits not in (32, 64):
+        raise ValueError("order keys are 32 or 64 bits")
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(rec) for _ in range(world)]
+    dist.all_gather(parts, rec, group=group)
+    g = torch.stack(parts)
+    valid = g[:, 1] >= 0
+    keys = g[:, 0] if key_bits == 64 else torch.div(g[:, 0], 1 << 32, rounding_mode="floor")
+    keys = torch.where(valid, keys, torch.full_like(keys, _I64_MIN))
+    best = keys.max()
+    idx = torch.where(valid & (keys == best), g[:, 1], torch.full_like(g[:, 1], _I64_MAX)).min()
+    if key_bits == 64:
+        word0 = best
+    else:
+        low = torch.where(idx <= MAX_PACKED_INDEX, MAX_PACKED_INDEX - idx, torch.zeros_like(idx))
+        word0 = best * (1 << 32) + low
+    any_valid = valid.any()
+    rec[0] = torch.where(any_valid, word0, torch.full_like(word0, _I64_MIN))
+    rec[1] = torch.where(any_valid, idx, torch.full_like(idx, -1))
+    return rec
+
+
 class ShardedReducer:
     """Per-rank reduction + one all_reduce per op.
 
@@ -156,11 +190,19 @@ class ShardedReducer:
         self._combine(REDUCE_SUM_I32, self.i32, dist.ReduceOp.SUM, stream)
         return self.i32
 
+    @property
+    def packed_argmax(self) -> bool:
+        """Global indices fit the packed key's 32 bits: argmax partials
+        combine with one all_reduce MAX; otherwise records are gathered."""
+        return self.n_total - 1 <= MAX_PACKED_INDEX
+
     def argmax_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
-        if self.n_total - 1 > MAX_PACKED_INDEX:
-            raise ValueError("sharded argmax packs 32-bit global indices: n_total must be <= 2^32")
         self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
-        self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
+        if self.packed_argmax:
+            self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
+        elif self.world > 1:
+            with self._on(stream):
+                combine_argmax_records(self.arg, 32, self.group)
         return self.arg
 
     def argmax_async(self, dtype: str, shard: torch.Tensor, stream=None) -> torch.Tensor:
@@ -172,8 +214,6 @@ class ShardedReducer:
             return self.argmax_f32_async(shard, stream)
         if dtype not in ARGMAX_TYPE_BYTES:
             raise ValueError(f"no max/argmax order for {dtype!r}")
-        if self.n_total - 1 > MAX_PACKED_INDEX:
-            raise ValueError("sharded argmax packs 32-bit global indices: n_total must be <= 2^32")
         key = ("argmax", dtype)
         if key not in self.typed_arg:
             self.typed_arg[key] = torch.zeros(2, dtype=torch.int64, device=self.device)
@@ -184,19 +224,11 @@ class ShardedReducer:
                                    workspace=self.workspace)
         if self.world == 1:
             return rec
-        if dtype != "f64":
+        if dtype != "f64" and self.packed_argmax:
             self._combine(key, rec[:1], dist.ReduceOp.MAX, stream)
             return rec
         with self._on(stream):
-            gathered = torch.empty(self.world * 2, dtype=torch.int64, device=self.device)
-            dist.all_gather_into_tensor(gathered, rec, group=self.group)
-            g = gathered.view(self.world, 2)
-            valid = g[:, 1] >= 0
-            keys = torch.where(valid, g[:, 0], torch.full_like(g[:, 0], -(1 << 63)))
-            best = keys.max()
-            idx = torch.where(valid & (keys == best), g[:, 1], torch.full_like(g[:, 1], (1 << 63) - 1)).min()
-            rec[0] = torch.where(valid.any(), best, torch.tensor(-(1 << 63), device=self.device))
-            rec[1] = torch.where(valid.any(), idx, torch.tensor(-1, device=self.device))
+            combine_argmax_records(rec, 64 if dtype == "f64" else 32, self.group)
         return rec
 
     def argmax(self, dtype: str, shard: torch.Tensor, stream=None) -> tuple[float | int, int]:
@@ -205,11 +237,12 @@ class ShardedReducer:
         if dtype == "f32":
             return self.argmax_result(rec)
         r = rec.cpu().numpy()
-        if dtype != "f64" and self.world > 1:
+        if dtype != "f64" and self.world > 1 and self.packed_argmax:
+            # after the all_reduce MAX only the packed word is global
             packed = int(r[0])
-            if packed == -(1 << 63):
+            if packed == _I64_MIN:
                 return float("nan"), -1
-            r = np.array([packed, 0xFFFFFFFF - (packed & 0xFFFFFFFF)], np.int64)
+            r = np.array([packed, MAX_PACKED_INDEX - (packed & MAX_PACKED_INDEX)], np.int64)
         return argmax_value(dtype, r)
 
     def _ordered_buffers(self, dtype: str) -> dict[str, torch.Tensor]:
@@ -301,10 +334,14 @@ class ShardedReducer:
 
     @staticmethod
     def argmax_result(arg: torch.Tensor) -> tuple[float, int]:
-        packed = int(arg[0].item())
-        if packed == -(1 << 63):
+        """(value, global index) of a combined f32 record: the packed word
+        carries both while the index fits 32 bits; beyond that the gathered
+        record's second word holds the index."""
+        packed, index = (int(v) for v in arg.tolist())
+        if packed == _I64_MIN:
             return float("nan"), -1
-        return unpack_argmax_key(packed)
+        value, packed_index = unpack_argmax_key(packed)
+        return value, index if index > MAX_PACKED_INDEX else packed_index
 
 
 def cpu_sharded_combine(partial_fn: Callable[[int, int, int], tuple[float, int, int]], n_total: int) -> tuple:

@@ -66,3 +66,23 @@ def test_two_gpu_sharded_reductions_match_oracle(tmp_path, n_total):
     for r in got["ordered"]:
         assert np.float64(r["f32"]).view(np.uint64) == np.float64(want_f32).view(np.uint64)
         assert np.float64(r["bf16"]).view(np.uint64) == np.float64(want_bf16).view(np.uint64)
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_two_gpu_argmax_past_32_bit_indices(tmp_path):
+    """2^32 + 2^20 + 7 elements: the partial records are gathered (the packed
+    key has no room for the index) and the lowest index of the maximum,
+    past 2^32 on rank 1, wins for f32 and bf16."""
+    out = tmp_path / "wide.json"
+    n_total = (1 << 32) + (1 << 20) + 7
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", str(HERE / "_sharded_wide_worker.py"), str(out),
+           str(n_total)]
+    proc = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    got = json.loads(out.read_text())
+    assert got["world"] == 2
+    for r in got["results"]:
+        assert r["f32"] == [1000.0, (1 << 32) + 50]
+        assert r["bf16"] == [1000.0, (1 << 32) + 50]

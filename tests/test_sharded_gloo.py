@@ -94,6 +94,75 @@ def test_gloo_u32_partials_wrap(world):
     assert all(v == want for v in results.values())
 
 
+# per-case, per-rank (key, global index) partials; index -1 = empty shard
+RECORD_CASES = {
+    32: [[(7, 5), (7, (1 << 32) + 9), (-3, (1 << 33) + 1)],           # tie: lowest index wins
+         [(-(1 << 31), (1 << 32) + 2), ((1 << 31) - 1, (1 << 34) + 7), (0, -1)],  # extreme keys, empty rank
+         [(0, -1), (0, -1), (0, -1)],                                   # all empty
+         [(5, (1 << 32) - 1), (5, 1 << 32), (4, 3)]],                   # the 32-bit boundary
+    64: [[(-(1 << 63) + 1, 4), (123456789012345, 77), (123456789012345, 76)],
+         [(0, -1), (-5, (1 << 40) + 3), (-5, (1 << 40) + 2)]],
+}
+
+
+def _record(bits: int, key: int, index: int) -> list[int]:
+    if index < 0:
+        return [-(1 << 63), -1]
+    if bits == 64:
+        return [key, index]
+    return [key * (1 << 32) + (0xFFFFFFFF - index if index <= 0xFFFFFFFF else 0), index]
+
+
+def _records_worker(rank: int, world: int, port: int, q):
+    import torch
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    out = {}
+    for bits, cases in RECORD_CASES.items():
+        for c, case in enumerate(cases):
+            rec = torch.tensor(_record(bits, *case[rank]), dtype=torch.int64)
+            sharded.combine_argmax_records(rec, bits)
+            out[(bits, c)] = rec.tolist()
+    q.put((rank, out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_argmax_records_beyond_32_bit_indices(world):
+    """The gathered-record combine (f64 keys, and arrays past 2^32
+    elements): largest key, lowest global index, empty shards skipped."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_records_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for bits, cases in RECORD_CASES.items():
+        for c, case in enumerate(cases):
+            live = [(k, i) for k, i in case[:world] if i >= 0]
+            if live:
+                best = max(k for k, _ in live)
+                want = _record(bits, best, min(i for k, i in live if k == best))
+            else:
+                want = [-(1 << 63), -1]
+            for rank in range(world):
+                assert results[rank][(bits, c)] == want, (bits, c, rank)
+
+
+def test_argmax_result_reads_wide_indices():
+    import torch
+    rec = torch.tensor(_record(32, 0x3F800000, (1 << 32) + 11), dtype=torch.int64)   # 1.0f at index 2^32 + 11
+    assert sharded.ShardedReducer.argmax_result(rec) == (1.0, (1 << 32) + 11)
+    rec = torch.tensor(_record(32, 0x3F800000, 12), dtype=torch.int64)
+    rec[1] = 99  # a stale local index after the packed all_reduce: the packed word decides
+    assert sharded.ShardedReducer.argmax_result(rec) == (1.0, 12)
+
+
 def test_sum_partial_types():
     import torch
     assert sharded.sum_partial_dtype("i32") == torch.int32
