@@ -451,8 +451,8 @@ def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
 
 def profile_run(which: str) -> None:
     """Small cases for ncu: each selected kernel 1 warm-up + 3 launches.
-    Inputs exceed L2 (126 MB) except the block sum, whose BASELINE size is
-    4 MiB; at most ~2.2 GB is on the device at once."""
+    Inputs exceed L2 (126 MB) except the block sum, whose benchmark size is
+    4 MiB (2^20 f32); at most ~2.2 GB is on the device at once."""
     import torch
 
     import flight4s_b200 as f4s
@@ -560,7 +560,7 @@ def profile_run(which: str) -> None:
 
 
 def kernel_table(ctx, hp, dev, peak) -> dict:
-    """The other hot-path kernels at their BASELINE configurations, 1 GPU,
+    """The other hot-path kernels at their benchmark configurations, 1 GPU,
     CUDA events around `reps` back-to-back launches after warm-up.  Every
     section allocates its own buffers after releasing the previous ones to
     the driver: carved out of one reused allocator segment, an input and an
