@@ -142,6 +142,21 @@ def test_host_buffer_bit_identical(ctx, hp, dtype, n):
     buf.close()
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "e5m2", "f64"])
+def test_host_buffer_pageable_odd_start(ctx, hp, dtype):
+    """Pageable host memory starting one element past an allocation: the
+    order fixes on the array, not on its host address."""
+    x = _values(dtype, 1_234_567, seed=31)
+    backing = np.concatenate([np.zeros(1, x.dtype), x])
+    view = backing[1:]
+    staging = ctx.allocate("u8", 256 + 2 * 2 * f4s.ORDERED_GROUP_BYTES)
+    s1, s2 = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    want, _ = orc.sum_ordered(dtype, x)
+    assert _bits(hp.reduce_host_sum(dtype, view, staging, s1, s2, policy="deterministic")) == _bits(want)
+    s1.close()
+    s2.close()
+
+
 def test_host_buffer_fast_and_integers(ctx, hp):
     """The fast policy and the integer sums keep the per-chunk pipeline."""
     x = _values("f32", 1_000_003, seed=4)
