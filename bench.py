@@ -364,6 +364,10 @@ def main() -> None:
     achieved = per_launch_bytes / (kernel_ms[dominant] / 1e3) / 1e9
     traffic_per_elem = _traffic_table().get(dominant)
     cpu = cpu_reference_run(1 << args.cpu_sample_log2, 3, 1, threads) if world == 1 and not args.no_cpu else None
+    if cpu is not None:
+        # the same port on one core, beside the all-core figure
+        one = cpu_reference_run(1 << max(args.cpu_sample_log2 - 2, 10), 1, 1, 1)
+        cpu["single_thread"] = {k: one[k] for k in ("value", "unit", "cores", "sample")}
     line = {
         "metric": "achieved HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -382,7 +386,8 @@ def main() -> None:
         "gpu_launches": 3 * args.steps * world,
         "clocks": clocks,
         "e2e": e2e,
-        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")} if cpu else None,
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "single_thread")}
+        if cpu else None,
         "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
