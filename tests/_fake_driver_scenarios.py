@@ -304,6 +304,17 @@ def host_ordered_pipeline():
         else:
             raise AssertionError("expected ValueError")
     assert count() == before
+    # Python-side checks: element size of the host array, unknown policy or type
+    for call, msg in [(lambda: hp.reduce_host_sum("f64", host, staging, 11, 12), "8-byte elements"),
+                      (lambda: hp.reduce_host_sum("f32", host, staging, 11, 12, policy="exact"), "unknown reduction policy"),
+                      (lambda: hp.reduce_host_sum("bool", host, staging, 11, 12), "no ReduceSum accumulator")]:
+        try:
+            call()
+        except ValueError as e:
+            assert msg in str(e), (str(e), msg)
+        else:
+            raise AssertionError("expected ValueError")
+    assert count() == before
     ctx.close()
 
 
