@@ -682,6 +682,27 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     del raw
     torch.cuda.empty_cache()  # next section on freshly allocated buffers
 
+    # ReduceSum of a pinned host array through the host-buffer call (PCIe
+    # host-to-device copies inside the call), fast and order-fixed; the call
+    # synchronizes its own two streams, so it is timed by the host clock
+    n = 1 << 28
+    hx = ctx.allocate_pinned("f32", n)
+    hx.array[:] = 1.0
+    staging = ctx.allocate("u8", 256 + 2 * (256 << 20))
+    s_copy, s_comp = ctx.create_stream(non_blocking=True), ctx.create_stream(non_blocking=True)
+    for policy in ("fast", "deterministic"):
+        for _ in range(2):
+            hp.reduce_host_sum("f32", hx.array, staging, s_copy, s_comp, policy=policy)
+        ts = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            hp.reduce_host_sum("f32", hx.array, staging, s_copy, s_comp, policy=policy)
+            ts.append(time.perf_counter() - t0)
+        row(f"host-buffer reduce_sum_f32 {policy} 1 GiB", 4 * n, n, sorted(ts)[2] * 1e3,
+            timing="host wall clock, median of 5 synchronous calls", bound="PCIe host-to-device")
+    for b in (s_copy, s_comp, staging, hx):
+        b.close()
+
     # elementwise Convert, 2^28 elements (f32 side 1 GiB)
     n = 1 << 28
     xf = torch.empty(n, dtype=torch.float32, device=dev)
