@@ -115,3 +115,27 @@ def test_unordered_types_rejected(ctx, hp):
         rc = _native.lib.f4s_reduce_argmax(hp.handle, 0, code, d.address, 8, d.address, ws.address, ws.size_bytes,
                                            0, 0)
         assert rc == _native.STATUS_INVALID_ARGUMENT and "no max/argmax order" in _native.last_status()[2]
+
+
+def test_full_size_against_torch(ctx, hp, torch_dev):
+    """Benchmark-scale arrays: the index and value of torch.argmax (its
+    first maximal element) on the same device data, many ties included
+    (normal bf16 / f16 repeat their largest values)."""
+    import torch
+    g = torch.Generator(device=torch_dev)
+    g.manual_seed(0xA5)
+    cases = [("f16", torch.float16, 1 << 31), ("bf16", torch.bfloat16, 1 << 31), ("i32", torch.int32, 1 << 32),
+             ("f64", torch.float64, 1 << 30)]
+    for dtype, tdt, n in cases:
+        if tdt == torch.int32:
+            x = torch.randint(-1000, 1001, (n,), dtype=torch.int32, device=torch_dev, generator=g)
+        else:
+            x = torch.randn(n, dtype=torch.float32 if tdt != torch.float64 else tdt, device=torch_dev,
+                            generator=g).to(tdt)
+        value, index = hp.reduce_argmax(dtype, x.view(torch.int16) if tdt in (torch.float16, torch.bfloat16) else x,
+                                        n=n)
+        want = int(torch.argmax(x).item())
+        assert index == want, (dtype, index, want)
+        assert value == x[want].item(), dtype
+        del x
+        torch.cuda.empty_cache()
