@@ -14,10 +14,27 @@ small partial, and the partials are combined by one collective:
 The partial kernels are the hot-path reductions; the collective is
 torch.distributed (NCCL over NVLink on GPUs; gloo in the CPU tests, where
 `partial_fn` supplies the per-rank partial instead of a kernel).
+
+Failure handling (the reference has one GPU per context and no collective,
+so this follows its host-side failure model: errors surface as exceptions
+on the host, nothing hangs):
+  * `RankMonitor` -- liveness through the process group's store: each rank
+    announces the step it is about to run, and before launching anything a
+    rank checks that every peer has announced that step.  A peer that left
+    (`leave()`) or fell silent raises `RankFailure` on the survivors, on
+    the host, before any kernel or collective of that step is queued.
+  * `PendingCollectives.wait_checked(timeout_s)` -- a bounded host wait on
+    the in-flight collectives: a collective that fails (a peer's
+    connection closed) or does not finish in time aborts the communicator
+    (`ProcessGroup.abort`, which for NCCL is ncclCommAbort) and raises
+    `CollectiveFailure` / `CollectiveTimeout`.  The NCCL backend's own
+    watchdog polls ncclCommGetAsyncError and enforces the process group's
+    timeout behind this.
 """
 from __future__ import annotations
 
 import contextlib
+import time
 from typing import Any, Callable, Optional
 
 import numpy as np
@@ -117,6 +134,143 @@ def combine_argmax_records(rec: torch.Tensor, key_bits: int, group: Any = None) 
     return rec
 
 
+class CollectiveFailure(RuntimeError):
+    """A collective of the sharded combine failed; its communicator has
+    been aborted and the process group must be destroyed and recreated."""
+
+
+class CollectiveTimeout(CollectiveFailure):
+    """A collective did not complete within its bound (a peer stopped
+    answering); the communicator has been aborted."""
+
+
+class RankFailure(RuntimeError):
+    """A peer rank left the job or stopped announcing steps; raised on the
+    host before this rank queues any work of the step."""
+
+
+def abort_group(group: Any = None) -> None:
+    """Abort the communicator of `group` (default: the world group) so no
+    rank blocks in it any longer.  For NCCL this is ncclCommAbort."""
+    pg = group if group is not None else dist.group.WORLD
+    try:
+        pg.abort()
+    except Exception:  # already aborted or torn down: nothing left to unblock
+        pass
+
+
+class PendingCollectives:
+    """The in-flight asynchronous all_reduces of a reducer, one per key.
+
+    `release(key)` orders the current stream after the key's previous
+    collective (its buffer is about to be rewritten), `wait()` orders the
+    current stream after all of them without blocking the host, and
+    `wait_checked(timeout_s)` blocks the host for at most `timeout_s`: a
+    collective that failed or is still running then aborts the
+    communicator and raises."""
+
+    def __init__(self, group: Any = None):
+        self.group = group
+        self._pending: dict[Any, Any] = {}
+
+    def __contains__(self, key: Any) -> bool:
+        return key in self._pending
+
+    def __len__(self) -> int:
+        return len(self._pending)
+
+    def start(self, key: Any, tensor: torch.Tensor, op: Any) -> None:
+        self._pending[key] = dist.all_reduce(tensor, op=op, group=self.group, async_op=True)
+
+    def release(self, key: Any) -> None:
+        prior = self._pending.pop(key, None)
+        if prior is not None:
+            prior.wait()
+
+    def wait(self) -> None:
+        for work in self._pending.values():
+            work.wait()
+        self._pending.clear()
+
+    def wait_checked(self, timeout_s: float, poll_s: float = 2e-4) -> None:
+        deadline = time.monotonic() + timeout_s
+        for key, work in list(self._pending.items()):
+            while not work.is_completed():
+                if time.monotonic() > deadline:
+                    self._pending.clear()
+                    abort_group(self.group)
+                    raise CollectiveTimeout(f"collective {key!r} did not complete within {timeout_s:g} s; "
+                                            "communicator aborted")
+                time.sleep(poll_s)
+            try:
+                work.wait()  # raises the collective's error, if it had one
+            except Exception as exc:
+                self._pending.clear()
+                abort_group(self.group)
+                raise CollectiveFailure(f"collective {key!r} failed: {exc}; communicator aborted") from exc
+        self._pending.clear()
+
+
+class RankMonitor:
+    """Host-side liveness of the ranks of a process group, through the
+    group's store (a TCP key-value store every rank reaches without the
+    communicator).  Each rank calls `enter_step(s)` before queuing the work
+    of step s: it announces s and returns once every peer has announced s,
+    or raises `RankFailure` if a peer has left (`leave()`) or has not
+    announced s within `timeout_s`.  A rank that stops between steps is
+    therefore noticed before anything of the next step is launched."""
+
+    def __init__(self, group: Any = None, timeout_s: float = 10.0, poll_s: float = 1e-3, prefix: str = "f4s/ranks",
+                 store: Any = None):
+        self.group = group
+        pg = group if group is not None else dist.group.WORLD
+        self.store = store if store is not None else pg.get_group_store()
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout_s = timeout_s
+        self.poll_s = poll_s
+        self.prefix = prefix
+        self.step = 0
+
+    def _key(self, what: str, rank: int) -> str:
+        return f"{self.prefix}/{what}/{rank}"
+
+    def enter_step(self, step: Optional[int] = None) -> int:
+        step = self.step + 1 if step is None else step
+        if step <= self.step:
+            raise ValueError(f"steps must increase: {step} after {self.step}")
+        try:
+            self.store.add(self._key("step", self.rank), step - self.step)
+        except Exception as exc:
+            raise RankFailure(f"rank liveness store unreachable before step {step}: {exc}") from exc
+        self.step = step
+        deadline = time.monotonic() + self.timeout_s
+        waiting = [r for r in range(self.world) if r != self.rank]
+        while waiting:
+            still = []
+            for r in waiting:
+                try:
+                    left = self.store.add(self._key("left", r), 0)
+                    reached = self.store.add(self._key("step", r), 0)
+                except Exception as exc:  # the store went away with the rank hosting it
+                    raise RankFailure(f"rank liveness store unreachable before step {step}: {exc}") from exc
+                if left:
+                    raise RankFailure(f"rank {r} left the job before step {step}")
+                if reached < step:
+                    still.append(r)
+            waiting = still
+            if waiting:
+                if time.monotonic() > deadline:
+                    raise RankFailure(f"rank(s) {waiting} did not reach step {step} within {self.timeout_s:g} s")
+                time.sleep(self.poll_s)
+        return step
+
+    def leave(self) -> None:
+        """Announce that this rank leaves between steps; peers raise
+        RankFailure at their next `enter_step`."""
+        self.store.add(self._key("left", self.rank), 1)
+
+
 class ShardedReducer:
     """Per-rank reduction + one all_reduce per op.
 
@@ -125,9 +279,16 @@ class ShardedReducer:
     kernel of the next (the three reductions are independent).  Each op has
     its own partial buffer; before a kernel overwrites it, the stream waits
     for that buffer's previous all_reduce.  Call `wait()` (device-side) before
-    reading results on `stream`; the `*_result` helpers do so."""
+    reading results on `stream`; the `*_result` helpers do so.
 
-    def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None, granule: int = 1):
+    Failure handling: `wait_checked(timeout_s)` bounds the host's wait for
+    the in-flight collectives (a failed or overdue one aborts the
+    communicator and raises `CollectiveFailure` / `CollectiveTimeout`), and
+    with a `monitor` (a `RankMonitor`) `begin_step()` raises `RankFailure`
+    before a step's first launch when a peer has left."""
+
+    def __init__(self, hotpath: Any, device: torch.device, n_total: int, group: Any = None, granule: int = 1,
+                 monitor: Optional[RankMonitor] = None):
         self.hp = hotpath
         self.device = device
         self.group = group
@@ -145,7 +306,8 @@ class ShardedReducer:
         self.typed_arg: dict[Any, torch.Tensor] = {}  # record of each typed argmax
         self._ordered: dict[str, dict[str, torch.Tensor]] = {}  # per-type buffers of order-fixed sums
         self._ordered_groups: dict[str, int] = {}  # this rank's group count per type
-        self._pending: dict[Any, Any] = {}
+        self._pending = PendingCollectives(group)
+        self.monitor = monitor
 
     @staticmethod
     def _on(stream: Optional[torch.cuda.Stream]):
@@ -156,10 +318,9 @@ class ShardedReducer:
     def _release(self, key: Any, shard: torch.Tensor, stream: Optional[torch.cuda.Stream]) -> None:
         if shard.numel() != self.count:
             raise ValueError(f"rank {self.rank} shard holds {shard.numel()} elements, expected {self.count}")
-        prior = self._pending.pop(key, None)
-        if prior is not None:
+        if key in self._pending:
             with self._on(stream):
-                prior.wait()  # the stream waits until that all_reduce has released the partial
+                self._pending.release(key)  # the stream waits until that all_reduce has released the partial
 
     def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
         self._release(op, shard, stream)
@@ -170,15 +331,31 @@ class ShardedReducer:
     def _combine(self, op: Any, tensor: torch.Tensor, reduce_op, stream: Optional[torch.cuda.Stream]) -> None:
         if self.world > 1:
             with self._on(stream):
-                self._pending[op] = dist.all_reduce(tensor, op=reduce_op, group=self.group, async_op=True)
+                self._pending.start(op, tensor, reduce_op)
 
     def wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         """Make `stream` (default: the current stream) wait for every
         outstanding all_reduce."""
         with self._on(stream):
-            for work in self._pending.values():
-                work.wait()
-        self._pending.clear()
+            self._pending.wait()
+
+    def wait_checked(self, timeout_s: float, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Block the host until every outstanding all_reduce has completed,
+        for at most `timeout_s`; a failed or overdue collective aborts the
+        communicator and raises CollectiveFailure / CollectiveTimeout."""
+        with self._on(stream):
+            self._pending.wait_checked(timeout_s)
+
+    def begin_step(self, step: Optional[int] = None) -> int:
+        """With a monitor: announce the next step and raise RankFailure if a
+        peer has left or not reached it (nothing of the step is queued yet).
+        Without one: a no-op returning 0."""
+        return self.monitor.enter_step(step) if self.monitor is not None else 0
+
+    def abort(self) -> None:
+        """Abort the communicator: in-flight collectives end with an error
+        on every rank instead of waiting for a peer that is gone."""
+        abort_group(self.group)
 
     def sum_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
         self._reduce(REDUCE_SUM_F32, shard, self.f64, stream)
