@@ -10,26 +10,34 @@
 // needs a small caller-provided workspace; this entry point needs none.
 //
 // How: the workspace lives in the file-scope device array below, 64 KiB
-// per GPU, created when this library's device code is first loaded on a GPU
-// and held by that GPU until the process exits.  Host code cannot use the
-// array's name as a device address (on the host it names a stand-in), so the
-// first call on each device makes that device's context current and asks
-// cudaGetSymbolAddress for the real address, which is cached per device.
-// Make that first call outside any stream capture.  The block-sum kernel is
-// the same one the regular entry point launches; only the workspace differs.
+// per GPU, created when this library's device code is first loaded into a
+// CUDA context and held until that context is destroyed (for the primary
+// context, until the process exits).  Host code cannot use the array's name
+// as a device address (on the host it names a stand-in), so the first call
+// in each context makes that context current and asks cudaGetSymbolAddress
+// for the real address, which is then cached under the context's unique id
+// (cuCtxGetId).  One device can carry several contexts (its primary context
+// and contexts made with cuCtxCreate), each with its own copy of the array,
+// and a destroyed context's id is never reused, so an address is only ever
+// used in the context it was looked up in.  That first call per context may
+// load this file's device code, which a stream capture cannot record: it is
+// rejected with F4S_STATUS_INVALID_ARGUMENT while `stream` is capturing, so
+// make it before any capture.  The block-sum kernel is the same one the
+// regular entry point launches; only the workspace differs.
 //
 // Limits and sharing: the workspace holds 256 bytes of header plus one
 // 4-byte partial per 65536-element cluster, so n may be at most
 // 16320 * 65536 = 1,069,547,520 elements; larger n is rejected with
-// F4S_STATUS_INVALID_ARGUMENT.  Every call on a device shares the one
+// F4S_STATUS_INVALID_ARGUMENT.  Every call in a context shares the one
 // array and the array keeps the last call's contents: each call first
-// zeroes the ticket counter with cudaMemsetAsync on its own stream, and
-// calls whose execution overlaps on the GPU (different streams, no
-// ordering between them) race on the array and give wrong results.
-// Nothing here calls cudaMalloc, cudaFree or any allocating routine.
+// zeroes the header (the ticket counter) on its own stream, and calls
+// whose execution overlaps on the GPU (different streams, no ordering
+// between them) race on the array and give wrong results.  Nothing here
+// calls cudaMalloc, cudaFree or any allocating routine.
 #include <cuda.h>
 #include <cuda_runtime_api.h>
 
+#include <limits>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -40,39 +48,67 @@
 namespace {
 
 constexpr std::size_t kNoallocWorkspaceBytes = 64 * 1024;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char f4s_noalloc_block_sum_workspace[kNoallocWorkspaceBytes];
 
+// Workspace addresses by context id.  A fixed table (no host allocation
+// either): when it is full the oldest entry is replaced, which only costs
+// that context one more symbol lookup on its next call.
+struct CachedAddress {
+  unsigned long long context_id = 0;
+  void* address = nullptr;
+};
+constexpr int kCachedContexts = 64;
 std::mutex g_setup_mutex;
-void* g_workspace_address[kMaxDevices] = {};
+CachedAddress g_cache[kCachedContexts];
+int g_next_slot = 0;
 
-// Device address of this device's workspace; `context` must be current.
-void* workspace_for_current_device() {
+// Device address of the workspace in the current context (the caller has
+// made the hot path's context current).  `stream` is the call's stream.
+void* workspace_for_current_context(CUstream stream) {
   const flight4s::cuda::DriverApi& api = flight4s::cuda::require_driver();
-  CUdevice device = 0;
-  if (api.cuCtxGetDevice(&device) != CUDA_SUCCESS || device < 0 || device >= kMaxDevices)
-    throw std::runtime_error("no usable current CUDA device for the allocation-free workspace");
+  CUcontext context = nullptr;
+  unsigned long long id = 0;
+  if (api.cuCtxGetCurrent(&context) != CUDA_SUCCESS || context == nullptr ||
+      api.cuCtxGetId(context, &id) != CUDA_SUCCESS)
+    throw std::runtime_error("no usable current CUDA context for the allocation-free workspace");
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_workspace_address[device] == nullptr) {
-    void* address = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&address, f4s_noalloc_block_sum_workspace);
-    if (err != cudaSuccess || address == nullptr) {
-      throw std::runtime_error(std::string("cudaGetSymbolAddress of the allocation-free workspace failed: ") +
-                               cudaGetErrorString(err));
-    }
-    g_workspace_address[device] = address;
+  for (const CachedAddress& entry : g_cache) {
+    if (entry.address != nullptr && entry.context_id == id) return entry.address;
   }
-  return g_workspace_address[device];
+  CUstreamCaptureStatus capture = CU_STREAM_CAPTURE_STATUS_NONE;
+  if (api.cuStreamIsCapturing(stream, &capture) != CUDA_SUCCESS || capture != CU_STREAM_CAPTURE_STATUS_NONE) {
+    throw std::invalid_argument(
+        "the first allocation-free block sum in a CUDA context looks up its workspace, which a stream capture "
+        "cannot record: make one call in this context before capturing");
+  }
+  void* address = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&address, f4s_noalloc_block_sum_workspace);
+  if (err != cudaSuccess || address == nullptr) {
+    throw std::runtime_error(std::string("cudaGetSymbolAddress of the allocation-free workspace failed: ") +
+                             cudaGetErrorString(err));
+  }
+  g_cache[g_next_slot] = CachedAddress{id, address};
+  g_next_slot = (g_next_slot + 1) % kCachedContexts;
+  return address;
 }
 
 }  // namespace
 
 namespace flight4s::cuda {
 
-// Largest n the static workspace can serve.
+// Largest n whose block-sum workspace fits the static array (the
+// workspace size grows with n).
 std::int64_t noalloc_block_sum_max_elements() {
-  return static_cast<std::int64_t>((kNoallocWorkspaceBytes - 256) / 4) * 65536;
+  static const std::int64_t largest = [] {
+    std::int64_t lo = 0, hi = std::numeric_limits<std::int32_t>::max();
+    while (lo < hi) {
+      const std::int64_t mid = lo + (hi - lo + 1) / 2;
+      if (Hotpath::block_sum_workspace_bytes(mid) <= kNoallocWorkspaceBytes) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }();
+  return largest;
 }
 
 CUresult block_sum_f32_noalloc(Hotpath& hp, CUstream stream, CUdeviceptr in, std::int32_t n,
@@ -85,12 +121,14 @@ CUresult block_sum_f32_noalloc(Hotpath& hp, CUstream stream, CUdeviceptr in, std
   }
   CurrentContextScope scope(hp.context());
   if (scope.push_result() != CUDA_SUCCESS) return scope.push_result();
-  void* ws = workspace_for_current_device();
+  void* ws = workspace_for_current_context(stream);
   // The kernel leaves the ticket at zero, but a call that never finished
-  // could not; clear it, ordered on this call's stream.
-  const cudaError_t err = cudaMemsetAsync(ws, 0, 256, reinterpret_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess)
-    throw std::runtime_error(std::string("clearing the allocation-free workspace failed: ") + cudaGetErrorString(err));
+  // could not; clear the header, ordered on this call's stream.
+  const CUresult cleared = require_driver().cuMemsetD8Async(reinterpret_cast<CUdeviceptr>(ws), 0, 256, stream);
+  if (cleared != CUDA_SUCCESS) {
+    scope.close();
+    return cleared;
+  }
   const CUresult r = hp.block_sum_f32(stream, in, n, partials, out, reinterpret_cast<CUdeviceptr>(ws),
                                       kNoallocWorkspaceBytes);
   const CUresult pop = scope.close();

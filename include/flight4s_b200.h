@@ -368,12 +368,14 @@ int f4s_block_reduce_sum_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in,
  * allocate device memory (a host whose device memory belongs to another
  * allocator, code running where allocation is not allowed, callers with no
  * way to keep a workspace).  No counterpart in the reference.  The
- * workspace is a 64 KiB static device array per GPU, held until the process
- * exits; n must be <= 1,069,547,520 (else F4S_STATUS_INVALID_ARGUMENT).
- * The first call on a device finds the array's device address with that
- * device's context current; make it outside any stream capture.  All calls
- * on a device share the array: calls that overlap on the GPU race.  Never
- * allocates. */
+ * workspace is a 64 KiB static device array in each CUDA context that loads
+ * the library's device code (a GPU's primary context holds it until the
+ * process exits); n must be <= 1,069,547,520 (else
+ * F4S_STATUS_INVALID_ARGUMENT).  The first call in a context finds the
+ * array's device address there and caches it under the context's id; that
+ * call is rejected (F4S_STATUS_INVALID_ARGUMENT) while `stream` is being
+ * captured, so make it before any capture.  All calls in a context share
+ * the array: calls that overlap on the GPU race.  Never allocates. */
 int f4s_block_reduce_sum_f32_noalloc(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, int32_t n,
                                      uint64_t partials, uint64_t out);
 

@@ -177,6 +177,8 @@ static CUresult f_set_current(CUcontext c) {
   return CUDA_SUCCESS;
 }
 static CUresult f_ctx_device(CUdevice* d) { *d = 0; return CUDA_SUCCESS; }
+static CUresult f_ctx_id(CUcontext c, unsigned long long* id) { *id = (unsigned long long)(uintptr_t)c; return CUDA_SUCCESS; }
+static CUresult f_stream_capturing(CUstream s, CUstreamCaptureStatus* st) { (void)s; *st = CU_STREAM_CAPTURE_STATUS_NONE; return CUDA_SUCCESS; }
 static CUresult f_ctx_sync(void) { INJECT(cuCtxSynchronize); return CUDA_SUCCESS; }
 static CUresult f_module_load(CUmodule* m, const void* image, unsigned n, CUjit_option* opts, void** vals) {
   (void)image;
@@ -293,6 +295,7 @@ static const Entry entries[] = {
     {"cuCtxGetCurrent", (void*)f_get_current},
     {"cuCtxSetCurrent", (void*)f_set_current},
     {"cuCtxGetDevice", (void*)f_ctx_device},
+    {"cuCtxGetId", (void*)f_ctx_id},
     {"cuCtxSynchronize", (void*)f_ctx_sync},
     {"cuModuleLoadDataEx", (void*)f_module_load},
     {"cuModuleUnload", (void*)f_module_unload},
@@ -306,6 +309,7 @@ static const Entry entries[] = {
     {"cuStreamDestroy", (void*)f_stream_destroy},
     {"cuStreamSynchronize", (void*)f_stream_sync},
     {"cuStreamWaitEvent", (void*)f_stream_wait},
+    {"cuStreamIsCapturing", (void*)f_stream_capturing},
     {"cuEventCreate", (void*)f_event_create},
     {"cuEventDestroy", (void*)f_event_destroy},
     {"cuEventRecord", (void*)f_event_record},

@@ -262,3 +262,11 @@ def test_invalid_arguments_rejected_before_the_driver():
     assert _native.lib.f4s_reduce_sum_f32(None, 0, 0, 0, 0, 0, 0, 0) == _native.STATUS_INVALID_ARGUMENT
     assert "hotpath handle must not be null" in _native.last_status()[2]
     assert _native.lib.f4s_block_reduce_workspace_bytes(1 << 20) == 256 + 4 * 16
+
+
+def test_block_sum_workspace_at_the_static_workspace_limit():
+    # 1,069,547,520 elements is the largest block sum whose workspace fits
+    # 64 KiB (the allocation-free entry point's static array); one more
+    # element needs another level-2 slot
+    assert _native.lib.f4s_block_reduce_workspace_bytes(1_069_547_520) == 64 * 1024
+    assert _native.lib.f4s_block_reduce_workspace_bytes(1_069_547_521) == 64 * 1024 + 4
