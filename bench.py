@@ -17,7 +17,12 @@ Rank 0 prints one JSON line.  `value` is device-resident whole-job GB/s
 (inputs already in HBM); `e2e` is the same step through the public
 host-buffer call (f4s_reduce_host: pinned host -> device copies inside the
 timed region).  At N = 1 the line also carries a per-kernel table for the
-other hot-path kernels (vectorAdd, block sum, softmax, RMSNorm, FP8).
+other hot-path kernels (vectorAdd, block sum, softmax, RMSNorm, FP8), the
+CPU baseline (the same passes and warm-up as the reference arm) and how far
+the f32 sum is from the reference's own Float fold on the same 2^32
+elements (`results.f32_sum_vs_reference_float_fold`).  For N > 1,
+`step_split` splits the step into kernel time and exposed collective time
+(the same launches timed without their collectives), per rank.
 `--impl reference` times the CPU restatement of the reference's path (the
 oracle port, all host threads) on a bounded sample of the same workload.
 """
@@ -202,7 +207,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel table")
     ap.add_argument("--cpu-sample-log2", type=int, default=28)
     ap.add_argument("--e2e-max-log2", type=int, default=30,
@@ -315,12 +320,53 @@ def main() -> None:
     # (for N > 1 the all_reduce runs on NCCL's stream, overlapping the next kernel)
     kernel_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / len(evs) for name, evs in kev.items()}
 
+    # N > 1: the same kernels without their collectives, timed the same way,
+    # so the step splits into kernel time and exposed collective time (each
+    # the max over ranks), plus every rank's own kernel times
+    step_split = None
+    if world > 1:
+        red.wait()
+        kout = torch.zeros(2, dtype=torch.int64, device=dev)
+        kops = [(f4s.REDUCE_SUM_F32, x), (f4s.REDUCE_ARGMAX_F32, x), (f4s.REDUCE_SUM_I32, xi)]
+
+        def kernels_only():
+            for op, buf in kops:
+                hp.reduce_into(op, buf, kout, n=count, stream=stream, index_base=offset, workspace=red.workspace)
+
+        for _ in range(2):
+            kernels_only()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ka.record(stream)
+        for _ in range(args.steps):
+            kernels_only()
+        kb.record(stream)
+        torch.cuda.synchronize()
+        mine = torch.tensor([ka.elapsed_time(kb) / args.steps, ms_local / args.steps]
+                            + [kernel_ms_local for kernel_ms_local in
+                               (sum(a.elapsed_time(b) for a, b in kev[name]) / len(kev[name]) for name, _ in ops)],
+                            dtype=torch.float64, device=dev)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        rows = torch.stack(every).cpu().tolist()
+        k_only = max(r[0] for r in rows)
+        step_split = {"kernels_only_ms_per_step": k_only, "step_ms": ms_step,
+                      "exposed_collective_ms_per_step": ms_step - k_only,
+                      "per_rank": [{"rank": i, "kernels_only_ms": r[0], "step_ms": r[1],
+                                    "kernel_ms_in_step": dict(zip([name for name, _ in ops], r[2:]))}
+                                   for i, r in enumerate(rows)],
+                      "how": "CUDA events on each rank's compute stream; kernels-only = the same three launches "
+                             "per step with no collectives"}
+
     # results of the last step (checked against torch on the full array at N = 1)
     red.wait()
     s_val = float(red.f64.item())
     i_val = int(red.i32.item())
     v_max, i_max = ShardedReducer.argmax_result(red.arg)
     verified = None
+    f32_parity = None
     if world == 1:
         ref_i = int(torch.sum(xi, dtype=torch.int64).item())
         ok_i = i_val == (ref_i + 2**31) % 2**32 - 2**31
@@ -329,6 +375,7 @@ def main() -> None:
         abs_s = torch.sum(x.abs(), dtype=torch.float64).item()
         ok_s = abs(s_val - ref_s) <= 1e-5 * abs_s
         verified = bool(ok_i and ok_a and ok_s)
+        f32_parity = reference_fold_gap(x, s_val, ref_s, abs_s) if not args.no_cpu else None
 
     peak, peak_kind = _peaks()
     bytes_step = 3 * 4 * N_TOTAL
@@ -363,7 +410,8 @@ def main() -> None:
     per_launch_bytes = 4 * count
     achieved = per_launch_bytes / (kernel_ms[dominant] / 1e3) / 1e9
     traffic_per_elem = _traffic_table().get(dominant)
-    cpu = cpu_reference_run(1 << args.cpu_sample_log2, 3, 1, threads) if world == 1 and not args.no_cpu else None
+    # the same passes and warm-up as the reference arm (bench.py --impl reference)
+    cpu = cpu_reference_run(1 << args.cpu_sample_log2, 20, 5, threads) if world == 1 and not args.no_cpu else None
     if cpu is not None:
         # the same port on one core, beside the all-core figure
         one = cpu_reference_run(1 << max(args.cpu_sample_log2 - 2, 10), 1, 1, 1)
@@ -382,7 +430,9 @@ def main() -> None:
                      "traffic": (traffic_per_elem * count) if traffic_per_elem else None,
                      "algorithmic_bytes_per_launch": per_launch_bytes,
                      "kernel_ms": kernel_ms},
-        "results": {"sum_f32": s_val, "sum_i32": i_val, "max_f32": v_max, "argmax": i_max, "verified_vs_torch": verified},
+        "results": {"sum_f32": s_val, "sum_i32": i_val, "max_f32": v_max, "argmax": i_max, "verified_vs_torch": verified,
+                    "f32_sum_vs_reference_float_fold": f32_parity},
+        "step_split": step_split,
         "gpu_launches": 3 * args.steps * world,
         "clocks": clocks,
         "e2e": e2e,
@@ -394,6 +444,32 @@ def main() -> None:
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def reference_fold_gap(x, ours: float, exact: float, abs_sum: float) -> dict:
+    """The f32 sum here against what the reference returns for the same
+    array: its F32 ReduceSum accumulates in Float
+    (core/src/main/scala/flight4s/core/types/CudaType.scala:216-218) and its
+    own check is Scala's Array[Float].sum, a sequential Float fold
+    (runtime/src/test/scala/flight4s/runtime/cuda/CudaResourcesJniSuite.scala:238).
+    The fold runs on the host over 256 MiB chunks copied back from the
+    device, carrying its Float accumulator; `exact` is torch's f64 sum of the
+    same device data.  Gaps are relative to sum|x|."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    t0 = time.perf_counter()
+    fold = 0.0
+    chunk = 1 << 26
+    for c in range(0, x.numel(), chunk):
+        fold = orc.sum_f32_sequential(x[c:c + chunk].cpu().numpy(), fold)
+    rounded = float(np.float32(ours))
+    return {"n": int(x.numel()), "ours_f64": ours, "ours_rounded_to_f32": rounded, "reference_float_fold": fold,
+            "exact": exact, "sum_abs": abs_sum,
+            "rel_gap_ours": abs(ours - exact) / abs_sum, "rel_gap_ours_rounded_f32": abs(rounded - exact) / abs_sum,
+            "rel_gap_reference_fold": abs(fold - exact) / abs_sum, "rel_gap_ours_f32_vs_fold": abs(rounded - fold) / abs_sum,
+            "fold_seconds": time.perf_counter() - t0,
+            "exact_is": "torch.sum(x, dtype=float64) on the device"}
 
 
 def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
@@ -449,6 +525,8 @@ def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
     return {"value": 3 * 4 * count * world / sec_step / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": 2 * 4 * count * world, "d2h_bytes_per_step": (8 + 16 + 4) * world,
             "ms_per_step": sec_step * 1e3, "steps": steps, "elements_per_rank": count,
+            "sample": f"{count} elements of each array per rank ({3 * 4 * count * world / 2**30:g} GiB of reduction "
+                      f"input per step over {world} GPU(s)) from pinned host memory, {steps} timed steps",
             "api": "f4s_reduce_host_sum_argmax_f32 + f4s_reduce_host (pinned host shard, chunked H2D "
                    "overlapped with the kernels; each host byte crosses PCIe once per step)",
             "bytes_counted": "3 reductions x 4 B x elements, as in value"}

@@ -339,7 +339,12 @@ int orc_vector_add_typed(int type_code, const void* a, const void* b, void* c, i
  * Scala's Array[Float].sum: a left fold in Float from 0.0f
  * (CudaResourcesJniSuite.scala:238). */
 float orc_sum_f32_sequential(const float* x, int64_t n) {
-  float acc = 0.0f;
+  return orc_sum_f32_sequential_from(x, n, 0.0f);
+}
+
+/* The same fold continued from a running Float accumulator, so an array
+ * can be folded chunk by chunk with the exact bits of one pass. */
+float orc_sum_f32_sequential_from(const float* x, int64_t n, float acc) {
   for (int64_t i = 0; i < n; ++i) acc += x[i];
   return acc;
 }

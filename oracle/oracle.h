@@ -33,6 +33,7 @@ void orc_vector_add_f32(const float* a, const float* b, float* c, int64_t n);
 void orc_vector_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int64_t n);
 
 float orc_sum_f32_sequential(const float* x, int64_t n);
+float orc_sum_f32_sequential_from(const float* x, int64_t n, float acc);
 double orc_sum_f32_exactish(const float* x, int64_t n, double* abs_sum);
 int32_t orc_sum_i32(const int32_t* x, int64_t n);
 int64_t orc_argmax_f32(const float* x, int64_t n, float* max_value);

@@ -51,6 +51,7 @@ def _load() -> C.CDLL:
         "orc_vector_add_f32": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_vector_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_sum_f32_sequential": (C.c_float, [C.c_void_p, C.c_int64]),
+        "orc_sum_f32_sequential_from": (C.c_float, [C.c_void_p, C.c_int64, C.c_float]),
         "orc_sum_f32_exactish": (C.c_double, [C.c_void_p, C.c_int64, P(C.c_double)]),
         "orc_sum_i32": (C.c_int32, [C.c_void_p, C.c_int64]),
         "orc_argmax_f32": (C.c_int64, [C.c_void_p, C.c_int64, P(C.c_float)]),
@@ -140,8 +141,9 @@ def vector_add_bf16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return c
 
 
-def sum_f32_sequential(x: np.ndarray) -> float:
-    return float(lib.orc_sum_f32_sequential(_p(x), x.size))
+def sum_f32_sequential(x: np.ndarray, acc: float = 0.0) -> float:
+    """Scala's Array[Float].sum (a Float left fold), continued from `acc`."""
+    return float(lib.orc_sum_f32_sequential_from(_p(x), x.size, np.float32(acc)))
 
 
 def sum_f32_exact(x: np.ndarray) -> tuple[float, float]:
