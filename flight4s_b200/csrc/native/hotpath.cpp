@@ -27,6 +27,10 @@ constexpr std::uint64_t kOrderedGroupOffset = 256;
 constexpr int kBlockSumThreads = 1024;
 constexpr int kBlockSumCluster = 8;
 constexpr std::int64_t kBlockSumElemsPerCluster = 256LL * 256LL;
+constexpr std::int64_t kBlockSumWarps = kBlockSumThreads / 32;
+// Arrays of at most this many 256-element tiles (2^23 elements) take the
+// cluster-free kernel (csrc/kernels/block_sum.cuh: kBlockSumCtaMaxTiles).
+constexpr std::int64_t kBlockSumCtaMaxTiles = 128LL * 256LL;
 constexpr int kAddBlock = 256;
 constexpr int kRowBlock = 256;
 constexpr int kFp8Threads = 256;
@@ -515,11 +519,17 @@ CUresult Hotpath::block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n,
   if (workspace_bytes < block_sum_workspace_bytes(n))
     throw std::invalid_argument("block-sum workspace too small: " + std::to_string(workspace_bytes) +
                                 " bytes, need " + std::to_string(block_sum_workspace_bytes(n)));
-  const int clusters = static_cast<int>(std::max<std::int64_t>(1, (static_cast<std::int64_t>(n) + kBlockSumElemsPerCluster - 1) / kBlockSumElemsPerCluster));
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;
   args.ptr(in).i32(n).ptr(partials).ptr(out).ptr(workspace);
+  const std::int64_t tiles = (static_cast<std::int64_t>(n) + 255) / 256;
+  if (tiles <= kBlockSumCtaMaxTiles) {
+    // small arrays: no cluster, every CTA takes a ticket (same tree, same bits)
+    const int ctas = static_cast<int>(std::max<std::int64_t>(1, (tiles + kBlockSumWarps - 1) / kBlockSumWarps));
+    return cur.finish(launch(function("f4s_block_reduce_sum_f32_cta"), stream, ctas, kBlockSumThreads, 0, args));
+  }
+  const int clusters = static_cast<int>(std::max<std::int64_t>(1, (static_cast<std::int64_t>(n) + kBlockSumElemsPerCluster - 1) / kBlockSumElemsPerCluster));
   return cur.finish(launch(function("f4s_block_reduce_sum_f32"), stream, clusters * kBlockSumCluster,
                            kBlockSumThreads, kBlockSumCluster, args));
 }

@@ -240,8 +240,16 @@ def hotpath_dispatch():
     assert count() == before
     parts = ctx.allocate("f32", 4096)
     ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
+    # up to 2^23 elements: the cluster-free kernel, one 1024-thread CTA per 32 tiles
     hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)
-    check("f4s_block_reduce_sum_f32", 128, block=1024, cluster=8)
+    check("f4s_block_reduce_sum_f32_cta", 128, block=1024)
+    hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1)
+    check("f4s_block_reduce_sum_f32_cta", 1, block=1024)
+    # above: clusters of 8 CTAs, one per 65536 elements
+    n_big = (1 << 23) + 1
+    ws_big = ctx.allocate("u8", hp.block_reduce_workspace_bytes(n_big))
+    hp.block_reduce_sum_f32_into(big, ctx.allocate("f32", (n_big + 255) // 256), out, ws_big, n=n_big)
+    check("f4s_block_reduce_sum_f32", 129 * 8, block=1024, cluster=8)
     ctx.close()
 
 

@@ -29,8 +29,9 @@ def test_reference_known_answer(ctx, hp):
     assert total == np.float32(896.0) and parts.tolist() == [896.0]
 
 
-@pytest.mark.parametrize("n", [0, 1, 2, 255, 256, 257, 65535, 65536, 65537, 1 << 20, (1 << 20) + 77,
-                               (1 << 24) + 5, (1 << 25) + 3])
+# up to 2^23 elements the cluster-free kernel runs, above it the cluster kernel
+@pytest.mark.parametrize("n", [0, 1, 2, 255, 256, 257, 8191, 8192, 8193, 65535, 65536, 65537, 1 << 20,
+                               (1 << 20) + 77, 1 << 23, (1 << 23) + 1, (1 << 24) + 5, (1 << 25) + 3])
 def test_bit_exact_vs_oracle(ctx, hp, n):
     x = orc.uniform_f32(n, seed=0x5EED + n)
     total, parts = _run(ctx, hp, x)
