@@ -213,6 +213,8 @@ def main() -> None:
     ap.add_argument("--e2e-max-log2", type=int, default=30,
                     help="cap on the per-rank host sample of each array in the e2e leg (pinned host memory)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch each reduction only after the previous kernel finished (no launch overlap)")
     ap.add_argument("--profile", default=None,
                     help="profiling mode: run one kernel (or 'all') a few times on a small case and exit")
     args = ap.parse_args()
@@ -276,13 +278,20 @@ def main() -> None:
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    ops = [("f4s_reduce_sum_f32", lambda: red.sum_f32_async(x, stream)),
-           ("f4s_reduce_argmax_f32", lambda: red.argmax_f32_async(x, stream)),
-           ("f4s_reduce_sum_i32", lambda: red.sum_i32_async(xi, stream))]
+    names = ["f4s_reduce_sum_f32", "f4s_reduce_argmax_f32", "f4s_reduce_sum_i32"]
 
+    def step():
+        # the three kernels back to back, their all_reduces (N > 1) after them
+        with red.batch(stream):
+            red.sum_f32_async(x, stream)
+            red.argmax_f32_async(x, stream)
+            red.sum_i32_async(xi, stream)
+
+    # Inputs are resident and no kernel writes them inside the step, so each
+    # reduction may start while the previous one finishes (launch overlap).
+    hp.set_launch_overlap(not args.no_overlap)
     for _ in range(args.warmup):
-        for _, op in ops:
-            op()
+        step()
     red.wait()
     # the GPUs the ranks use, by UUID (CUDA's device order need not be NVML's)
     sampler = ClockSampler(",".join(_gpu_uuid(i) for i in range(world))) if rank == 0 else None
@@ -290,18 +299,11 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     time.sleep(0.3)  # let the sampler start
-    # per-kernel events inside the timed region (the kernel-only roofline)
-    kev = {name: [] for name, _ in ops}
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_host0 = time.time()
     start.record(stream)
     for _ in range(args.steps):
-        for name, op in ops:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            op()
-            b.record(stream)
-            kev[name].append((a, b))
+        step()
     red.wait(stream)  # the last collectives belong to the timed region
     end.record(stream)
     torch.cuda.synchronize()
@@ -316,19 +318,33 @@ def main() -> None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_total = float(ms_t.item())
     ms_step = ms_total / args.steps
-    # per-kernel average: events on the compute stream bracket the kernel
-    # (for N > 1 the all_reduce runs on NCCL's stream, overlapping the next kernel)
-    kernel_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / len(evs) for name, evs in kev.items()}
+
+    # Each kernel alone: the same launches with events around each and no
+    # overlap (an event between two kernels ends their overlap), after the
+    # timed region; the per-kernel breakdown beside the step's figure.
+    red.wait()
+    hp.set_launch_overlap(False)
+    kout = torch.zeros(2, dtype=torch.int64, device=dev)
+    kops = [(f4s.REDUCE_SUM_F32, x), (f4s.REDUCE_ARGMAX_F32, x), (f4s.REDUCE_SUM_I32, xi)]
+    kev = {name: [] for name in names}
+    torch.cuda.synchronize()
+    for rep in range(4 if world == 1 else 10):
+        for name, (op, buf) in zip(names, kops):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            hp.reduce_into(op, buf, kout, n=count, stream=stream, index_base=offset, workspace=red.workspace)
+            b.record(stream)
+            if rep > 0:
+                kev[name].append((a, b))
+    torch.cuda.synchronize()
+    kernel_ms_alone = {name: sum(a.elapsed_time(b) for a, b in evs) / len(evs) for name, evs in kev.items()}
+    hp.set_launch_overlap(not args.no_overlap)
 
     # N > 1: the same kernels without their collectives, timed the same way,
     # so the step splits into kernel time and exposed collective time (each
-    # the max over ranks), plus every rank's own kernel times
+    # the max over ranks), plus every rank's own figures
     step_split = None
     if world > 1:
-        red.wait()
-        kout = torch.zeros(2, dtype=torch.int64, device=dev)
-        kops = [(f4s.REDUCE_SUM_F32, x), (f4s.REDUCE_ARGMAX_F32, x), (f4s.REDUCE_SUM_I32, xi)]
-
         def kernels_only():
             for op, buf in kops:
                 hp.reduce_into(op, buf, kout, n=count, stream=stream, index_base=offset, workspace=red.workspace)
@@ -345,9 +361,7 @@ def main() -> None:
         kb.record(stream)
         torch.cuda.synchronize()
         mine = torch.tensor([ka.elapsed_time(kb) / args.steps, ms_local / args.steps]
-                            + [kernel_ms_local for kernel_ms_local in
-                               (sum(a.elapsed_time(b) for a, b in kev[name]) / len(kev[name]) for name, _ in ops)],
-                            dtype=torch.float64, device=dev)
+                            + [kernel_ms_alone[name] for name in names], dtype=torch.float64, device=dev)
         every = [torch.empty_like(mine) for _ in range(world)]
         dist.all_gather(every, mine)
         rows = torch.stack(every).cpu().tolist()
@@ -355,13 +369,14 @@ def main() -> None:
         step_split = {"kernels_only_ms_per_step": k_only, "step_ms": ms_step,
                       "exposed_collective_ms_per_step": ms_step - k_only,
                       "per_rank": [{"rank": i, "kernels_only_ms": r[0], "step_ms": r[1],
-                                    "kernel_ms_in_step": dict(zip([name for name, _ in ops], r[2:]))}
+                                    "kernel_ms_alone": dict(zip(names, r[2:]))}
                                    for i, r in enumerate(rows)],
                       "how": "CUDA events on each rank's compute stream; kernels-only = the same three launches "
-                             "per step with no collectives"}
+                             "per step (same launch overlap) with no collectives"}
 
     # results of the last step (checked against torch on the full array at N = 1)
     red.wait()
+    hp.set_launch_overlap(False)  # the rest (e2e, the kernel table) launches each kernel on its own
     s_val = float(red.f64.item())
     i_val = int(red.i32.item())
     v_max, i_max = ShardedReducer.argmax_result(red.arg)
@@ -406,9 +421,13 @@ def main() -> None:
         return
 
     clocks = sampler.summary() if sampler else None
-    dominant = max(kernel_ms, key=kernel_ms.get)
+    # the three launches of a step are equal in size and run back to back,
+    # overlapping start and finish: each one's average duration is a third
+    # of the step (CUDA events on the launching stream over the timed region)
+    per_launch_ms = ms_local / args.steps / 3
+    dominant = max(kernel_ms_alone, key=kernel_ms_alone.get)
     per_launch_bytes = 4 * count
-    achieved = per_launch_bytes / (kernel_ms[dominant] / 1e3) / 1e9
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     traffic_per_elem = _traffic_table().get(dominant)
     # the same passes and warm-up as the reference arm (bench.py --impl reference)
     cpu = cpu_reference_run(1 << args.cpu_sample_log2, 20, 5, threads) if world == 1 and not args.no_cpu else None
@@ -423,13 +442,18 @@ def main() -> None:
         "elements_per_s": elements_s, "hbm_fraction": value / (peak * world),
         "config": {"workload": "full-array sum f32 + max/argmax f32 + sum i32, n=2^32 each, sharded over GPUs",
                    "n_total": N_TOTAL, "n_per_gpu": count, "parallelism": f"shard{world} + nccl all_reduce",
+                   "launch_overlap": not args.no_overlap,
                    "l2": "inputs 16 GiB per array >> 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": " + ".join(names) + " (three equal launches per step, each "
+                     "starting while the previous one finishes)", "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} hbm_gbs (copy) of MEASURED_PEAKS.json" if peak_kind == "measured"
                      else "fallback 6.65 TB/s", "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (traffic_per_elem * count) if traffic_per_elem else None,
+                     "traffic_kernel": dominant,
                      "algorithmic_bytes_per_launch": per_launch_bytes,
-                     "kernel_ms": kernel_ms},
+                     "launch_ms": per_launch_ms,
+                     "kernel_ms_alone": kernel_ms_alone,
+                     "frac_alone": {k: per_launch_bytes / (v / 1e3) / 1e9 / peak for k, v in kernel_ms_alone.items()}},
         "results": {"sum_f32": s_val, "sum_i32": i_val, "max_f32": v_max, "argmax": i_max, "verified_vs_torch": verified,
                     "f32_sum_vs_reference_float_fold": f32_parity},
         "step_split": step_split,
@@ -535,7 +559,8 @@ def run_e2e(ctx, hp, red, x, xi, count, world, dev, steps, barrier) -> dict:
 def profile_run(which: str) -> None:
     """Small cases for ncu: each selected kernel 1 warm-up + 3 launches.
     Inputs exceed L2 (126 MB) except the block sum, whose benchmark size is
-    4 MiB (2^20 f32); at most ~2.2 GB is on the device at once."""
+    4 MiB (2^20 f32); the row ops and FP8 run at their benchmark shapes
+    (32768 x 8192, 16384 x 16384); at most ~2.2 GB is on the device at once."""
     import torch
 
     import flight4s_b200 as f4s
@@ -613,7 +638,7 @@ def profile_run(which: str) -> None:
         o = torch.empty(1, dtype=torch.float32, device=dev)
         ws = torch.zeros(hp.block_reduce_workspace_bytes(m), dtype=torch.uint8, device=dev)
         rep(lambda: hp.block_reduce_sum_f32_into(x, parts, o, ws))
-    rows, cols = 8192, 8192
+    rows, cols = 32768, 8192  # the row-op benchmark shape: 512 MiB in, 512 MiB out
     if want("softmax") or want("rmsnorm"):
         xb = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)
         yb = torch.empty_like(xb)
@@ -626,6 +651,7 @@ def profile_run(which: str) -> None:
             rep(lambda: hp.rmsnorm_rows_bf16(xb, w, yb, rows, cols, 1e-6))
         del xb, yb
     if want("fp8_quant") or want("fp8_dequant"):
+        rows = cols = 16384  # the FP8 benchmark shape
         m = rows * cols
         xb = torch.empty(m, dtype=torch.bfloat16, device=dev)
         hp.fill_synthetic(xb, m, f4s.NORMAL_BF16_OUTLIERS, seed=SEED, p0=0.0, p1=2.0, p2=1e-3, p3=50.0)

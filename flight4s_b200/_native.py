@@ -65,6 +65,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "f4s_hotpath_module": (u64, [vp]),
     "f4s_hotpath_sm_count": (C.c_int, [vp]),
     "f4s_hotpath_set_reduce_cluster": (C.c_int, [vp, i32]),
+    "f4s_hotpath_set_launch_overlap": (C.c_int, [vp, i32]),
     "f4s_hotpath_wait_timeouts": (C.c_int, [vp, P(u32), i32]),
     "f4s_hotpath_check_bounded_wait": (C.c_int, [vp, u32]),
     "f4s_reduce_workspace_bytes": (u64, [vp]),

@@ -447,6 +447,11 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
   __shared__ Partial cluster_partials[kReduceMaxCluster];
   __shared__ int is_last;
 
+  // A kernel launched after this one as a programmatic dependent (launch
+  // overlap, off unless the host asks) may start once every CTA here has
+  // started; without such a launch this has no effect.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint64_t nthreads = static_cast<uint64_t>(gridDim.x) * blockDim.x;
 
@@ -497,6 +502,12 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
     }
     if (count > 0) Op::body(t, v, base, kWarp, count);
   }
+
+  // Launched as a programmatic dependent, this kernel may have streamed its
+  // input while the previous kernel on the stream was finishing: wait for
+  // that kernel (complete, its writes visible) before touching the workspace
+  // and the output, which it may share.  A no-op for an ordinary launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // thread -> warp -> CTA
   Partial p = Op::warp_merge(Op::finish(t, head));

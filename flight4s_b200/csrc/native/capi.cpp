@@ -374,6 +374,13 @@ int f4s_hotpath_set_reduce_cluster(f4s_hotpath* hotpath, int32_t cluster) {
   return guarded([&] { return op_status(hot(hotpath).set_reduce_cluster(cluster)); });
 }
 
+int f4s_hotpath_set_launch_overlap(f4s_hotpath* hotpath, int32_t enable) {
+  return guarded([&] {
+    hot(hotpath).set_launch_overlap(enable != 0);
+    return 0;
+  });
+}
+
 int f4s_hotpath_wait_timeouts(f4s_hotpath* hotpath, uint32_t* count, int32_t reset) {
   return guarded([&] {
     require_out(count, "timeout count");

@@ -15,7 +15,7 @@ void validate(const CudaLaunchRequest& request) {
 
 }  // namespace
 
-CUresult launch_in_current_context(const DriverApi& api, const CudaLaunchRequest& request) {
+CUresult launch_in_current_context(const DriverApi& api, const CudaLaunchRequest& request, bool programmatic) {
   validate(request);
   auto pointers = build_argument_pointers(request.arguments);
   const LaunchGeometry& g = request.geometry;
@@ -28,14 +28,23 @@ CUresult launch_in_current_context(const DriverApi& api, const CudaLaunchRequest
   config.blockDimZ = static_cast<unsigned>(g.block_z);
   config.sharedMemBytes = static_cast<unsigned>(g.dynamic_shared_memory_bytes);
   config.hStream = request.stream;
-  CUlaunchAttribute cluster{};
+  CUlaunchAttribute attrs[2]{};
+  unsigned count = 0;
   if (g.uses_cluster) {
-    cluster.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    cluster.value.clusterDim.x = static_cast<unsigned>(g.cluster_x);
-    cluster.value.clusterDim.y = static_cast<unsigned>(g.cluster_y);
-    cluster.value.clusterDim.z = static_cast<unsigned>(g.cluster_z);
-    config.attrs = &cluster;
-    config.numAttrs = 1;
+    attrs[count].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attrs[count].value.clusterDim.x = static_cast<unsigned>(g.cluster_x);
+    attrs[count].value.clusterDim.y = static_cast<unsigned>(g.cluster_y);
+    attrs[count].value.clusterDim.z = static_cast<unsigned>(g.cluster_z);
+    ++count;
+  }
+  if (programmatic) {
+    attrs[count].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attrs[count].value.programmaticStreamSerializationAllowed = 1;
+    ++count;
+  }
+  if (count > 0) {
+    config.attrs = attrs;
+    config.numAttrs = count;
   }
   return api.cuLaunchKernelEx(&config, request.function, pointers.empty() ? nullptr : pointers.data(),
                               nullptr);

@@ -28,7 +28,11 @@ class CudaLauncher final {
 
 // The same launch without the context push/pop, for callers that already
 // made `request.context` current (the hot-path entry points do, once per
-// call).  Returns the raw CUresult.
-CUresult launch_in_current_context(const DriverApi& api, const CudaLaunchRequest& request);
+// call).  Returns the raw CUresult.  `programmatic` adds programmatic
+// stream serialization (the kernel may start while the previous kernel on
+// the stream finishes; it must wait with griddepcontrol.wait before using
+// anything that kernel writes).
+CUresult launch_in_current_context(const DriverApi& api, const CudaLaunchRequest& request,
+                                   bool programmatic = false);
 
 }  // namespace flight4s::cuda

@@ -328,19 +328,20 @@ std::uint64_t Hotpath::block_sum_workspace_bytes(std::int64_t n) {
   return 256 + 4 * static_cast<std::uint64_t>(clusters);
 }
 
-CUresult Hotpath::launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args) {
+CUresult Hotpath::launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args,
+                         bool programmatic) {
   const DriverApi& api = require_driver();
   CudaLaunchRequest request{
       context_, fn, stream,
       LaunchGeometry{grid, 1, 1, block, 1, 1, 0, cluster > 0, cluster > 0 ? cluster : 0,
                      cluster > 0 ? 1 : 0, cluster > 0 ? 1 : 0},
       args.layout()};
-  return launch_in_current_context(api, request);
+  return launch_in_current_context(api, request, programmatic);
 }
 
-CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
-                         CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
-                         int accumulate) {
+CUresult Hotpath::reduce_launch(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                                CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
+                                int accumulate, bool programmatic) {
   const char* name = reduce_kernel_name(op);
   const int elem = reduce_input_bytes(op);
   if (n > 0) require_ptr(in, "input buffer");
@@ -372,7 +373,7 @@ CUresult Hotpath::reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint
   args.ptr(in).u32(static_cast<std::uint32_t>(n)).u32(static_cast<std::uint32_t>(n >> 32)).ptr(out).ptr(workspace)
       .u32(static_cast<std::uint32_t>(index_base)).u32(static_cast<std::uint32_t>(index_base >> 32))
       .i32(accumulate ? 1 : 0);
-  return cur.finish(launch(function(name), stream, clusters * cluster, kReduceBlock, cluster, args));
+  return cur.finish(launch(function(name), stream, clusters * cluster, kReduceBlock, cluster, args, programmatic));
 }
 
 namespace {
@@ -809,8 +810,8 @@ CUresult Hotpath::reduce_host_ops(const ReduceOp* ops, int nops, const void* hos
         // every op reduces the same staged chunk (one transfer, nops kernels)
         CUresult r = CUDA_SUCCESS;
         for (int i = 0; i < nops && r == CUDA_SUCCESS; ++i)
-          r = reduce(ops[i], compute_stream, buf, count, result_slot(i), workspace, workspace_bytes,
-                     index_base + first, k > 0 ? 1 : 0);
+          r = reduce_launch(ops[i], compute_stream, buf, count, result_slot(i), workspace, workspace_bytes,
+                            index_base + first, k > 0 ? 1 : 0, false);
         return r;
       },
       [&] {

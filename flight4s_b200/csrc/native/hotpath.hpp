@@ -86,13 +86,22 @@ class Hotpath {
   const HotpathShape& shape() const { return shape_; }
   // Re-size the full-array reduction grid for a cluster size in [1, 8].
   CUresult set_reduce_cluster(int cluster);
+  // Let each full-array reduction start streaming its input while the
+  // kernel launched before it on the same stream finishes (programmatic
+  // dependent launch); it waits for that kernel before touching its
+  // workspace or output.  Off by default; only for callers whose reduction
+  // inputs are never written by the kernel launched right before them.
+  void set_launch_overlap(bool enable) { overlap_ = enable; }
+  bool launch_overlap() const { return overlap_; }
 
   std::uint64_t reduce_workspace_bytes() const;
   static std::uint64_t block_sum_workspace_bytes(std::int64_t n);
 
   CUresult reduce(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
                   CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
-                  int accumulate);
+                  int accumulate) {
+    return reduce_launch(op, stream, in, n, out, workspace, workspace_bytes, index_base, accumulate, overlap_);
+  }
   // Order-fixed floating-point sums: 256 KiB groups of the 16-byte-aligned
   // body, group partials in `workspace` from byte 256 (f64 each, readable
   // after the launch), total = fixed tree over the group partials + the
@@ -168,7 +177,14 @@ class Hotpath {
 
  private:
   Hotpath() = default;
-  CUresult launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args);
+  CUresult launch(CUfunction fn, CUstream stream, int grid, int block, int cluster, ArgumentPack& args,
+                  bool programmatic = false);
+  // reduce(); `programmatic` launches it as a programmatic dependent of the
+  // previous kernel on `stream` (the host-buffer pipelines never do: their
+  // inputs arrive by copies).
+  CUresult reduce_launch(ReduceOp op, CUstream stream, CUdeviceptr in, std::uint64_t n, CUdeviceptr out,
+                         CUdeviceptr workspace, std::uint64_t workspace_bytes, std::uint64_t index_base,
+                         int accumulate, bool programmatic);
   // Chunked, double-buffered host->device pipeline shared by the host-buffer
   // reductions: every op in `ops` reduces each staged chunk, op i into
   // `host_outs[i]`.
@@ -190,6 +206,7 @@ class Hotpath {
   CUmodule module_ = nullptr;
   int sm_count_ = 0;
   HotpathShape shape_;
+  bool overlap_ = false;
 };
 
 }  // namespace flight4s::cuda

@@ -178,6 +178,14 @@ class Hotpath:
     def set_reduce_cluster(self, cluster: int) -> None:
         check(lib.f4s_hotpath_set_reduce_cluster(self._h, cluster), "reduction cluster size")
 
+    def set_launch_overlap(self, enable: bool) -> None:
+        """Let each device-resident full-array reduction start streaming its
+        input while the kernel launched before it on the same stream
+        finishes (programmatic dependent launch).  Only for callers that
+        never launch a kernel writing a reduction's input immediately before
+        that reduction on the same stream."""
+        check(lib.f4s_hotpath_set_launch_overlap(self._h, 1 if enable else 0), "launch overlap")
+
     def close(self) -> None:
         if self._h is not None:
             for b in (self._workspace, self._ordered_workspace, self._result):

@@ -281,6 +281,13 @@ class ShardedReducer:
     for that buffer's previous all_reduce.  Call `wait()` (device-side) before
     reading results on `stream`; the `*_result` helpers do so.
 
+    Inside `batch()` the kernels of several ops are queued back to back and
+    their all_reduces start together when the block ends; the f32 sum, i32
+    sum and f32 argmax then alternate between two partial buffers, so the
+    next batch's kernels never wait for this batch's collectives.  With the
+    hot path's launch overlap on, consecutive kernels of a batch also
+    overlap each other's start and finish (nothing is recorded between them).
+
     Failure handling: `wait_checked(timeout_s)` bounds the host's wait for
     the in-flight collectives (a failed or overdue one aborts the
     communicator and raises `CollectiveFailure` / `CollectiveTimeout`), and
@@ -298,9 +305,12 @@ class ShardedReducer:
         self.granule = granule
         self.offset, self.count = shard_bounds(n_total, self.world, self.rank, granule)
         self.counts = [shard_bounds(n_total, self.world, r, granule)[1] for r in range(self.world)]
-        self.f64 = torch.zeros(1, dtype=torch.float64, device=device)
-        self.i32 = torch.zeros(1, dtype=torch.int32, device=device)
-        self.arg = torch.zeros(2, dtype=torch.int64, device=device)
+        # two partial buffers per op; `_cur` is the one written last
+        self._partials = {REDUCE_SUM_F32: [torch.zeros(1, dtype=torch.float64, device=device) for _ in range(2)],
+                          REDUCE_SUM_I32: [torch.zeros(1, dtype=torch.int32, device=device) for _ in range(2)],
+                          REDUCE_ARGMAX_F32: [torch.zeros(2, dtype=torch.int64, device=device) for _ in range(2)]}
+        self._cur = {op: 0 for op in self._partials}
+        self._deferred: Optional[list] = None  # collectives queued inside batch()
         self.workspace = torch.zeros(hotpath.workspace_bytes, dtype=torch.uint8, device=device)
         self.typed: dict[str, torch.Tensor] = {}  # partial of each typed sum
         self.typed_arg: dict[Any, torch.Tensor] = {}  # record of each typed argmax
@@ -308,6 +318,43 @@ class ShardedReducer:
         self._ordered_groups: dict[str, int] = {}  # this rank's group count per type
         self._pending = PendingCollectives(group)
         self.monitor = monitor
+
+    @property
+    def f64(self) -> torch.Tensor:
+        """The f32 sum's partial (after wait(): the combined sum) of the last launch."""
+        return self._partials[REDUCE_SUM_F32][self._cur[REDUCE_SUM_F32]]
+
+    @property
+    def i32(self) -> torch.Tensor:
+        return self._partials[REDUCE_SUM_I32][self._cur[REDUCE_SUM_I32]]
+
+    @property
+    def arg(self) -> torch.Tensor:
+        return self._partials[REDUCE_ARGMAX_F32][self._cur[REDUCE_ARGMAX_F32]]
+
+    def _target(self, op: int) -> tuple[Any, torch.Tensor]:
+        """(pending key, buffer) the next launch of `op` writes.  In a batch
+        it is the buffer not written last time, whose collective (two
+        batches back) has long finished; otherwise the same buffer."""
+        idx = self._cur[op] ^ 1 if self._deferred is not None else self._cur[op]
+        self._cur[op] = idx
+        return (op, idx), self._partials[op][idx]
+
+    @contextlib.contextmanager
+    def batch(self, stream: Optional[torch.cuda.Stream] = None):
+        """Queue several reductions on `stream` back to back and start their
+        all_reduces together when the block ends (see the class notes)."""
+        if self._deferred is not None:
+            raise RuntimeError("batches do not nest")
+        self._deferred = []
+        try:
+            yield self
+        finally:
+            deferred, self._deferred = self._deferred, None
+            if self.world > 1:
+                with self._on(stream):
+                    for key, tensor, reduce_op in deferred:
+                        self._pending.start(key, tensor, reduce_op)
 
     @staticmethod
     def _on(stream: Optional[torch.cuda.Stream]):
@@ -322,14 +369,11 @@ class ShardedReducer:
             with self._on(stream):
                 self._pending.release(key)  # the stream waits until that all_reduce has released the partial
 
-    def _reduce(self, op: int, shard: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream]):
-        self._release(op, shard, stream)
-        self.hp.reduce_into(op, shard, out, n=self.count,
-                            stream=stream if stream is not None else torch.cuda.current_stream(),
-                            index_base=self.offset, workspace=self.workspace)
-
     def _combine(self, op: Any, tensor: torch.Tensor, reduce_op, stream: Optional[torch.cuda.Stream]) -> None:
         if self.world > 1:
+            if self._deferred is not None:
+                self._deferred.append((op, tensor, reduce_op))
+                return
             with self._on(stream):
                 self._pending.start(op, tensor, reduce_op)
 
@@ -357,15 +401,23 @@ class ShardedReducer:
         on every rank instead of waiting for a peer that is gone."""
         abort_group(self.group)
 
+    def _reduce_partial(self, op: int, shard: torch.Tensor, stream) -> tuple[Any, torch.Tensor]:
+        key, out = self._target(op)
+        self._release(key, shard, stream)
+        self.hp.reduce_into(op, shard, out, n=self.count,
+                            stream=stream if stream is not None else torch.cuda.current_stream(),
+                            index_base=self.offset, workspace=self.workspace)
+        return key, out
+
     def sum_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
-        self._reduce(REDUCE_SUM_F32, shard, self.f64, stream)
-        self._combine(REDUCE_SUM_F32, self.f64, dist.ReduceOp.SUM, stream)
-        return self.f64
+        key, out = self._reduce_partial(REDUCE_SUM_F32, shard, stream)
+        self._combine(key, out, dist.ReduceOp.SUM, stream)
+        return out
 
     def sum_i32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
-        self._reduce(REDUCE_SUM_I32, shard, self.i32, stream)
-        self._combine(REDUCE_SUM_I32, self.i32, dist.ReduceOp.SUM, stream)
-        return self.i32
+        key, out = self._reduce_partial(REDUCE_SUM_I32, shard, stream)
+        self._combine(key, out, dist.ReduceOp.SUM, stream)
+        return out
 
     @property
     def packed_argmax(self) -> bool:
@@ -374,13 +426,13 @@ class ShardedReducer:
         return self.n_total - 1 <= MAX_PACKED_INDEX
 
     def argmax_f32_async(self, shard: torch.Tensor, stream=None) -> torch.Tensor:
-        self._reduce(REDUCE_ARGMAX_F32, shard, self.arg, stream)
+        key, out = self._reduce_partial(REDUCE_ARGMAX_F32, shard, stream)
         if self.packed_argmax:
-            self._combine(REDUCE_ARGMAX_F32, self.arg[:1], dist.ReduceOp.MAX, stream)
+            self._combine(key, out[:1], dist.ReduceOp.MAX, stream)
         elif self.world > 1:
             with self._on(stream):
-                combine_argmax_records(self.arg, 32, self.group)
-        return self.arg
+                combine_argmax_records(out, 32, self.group)
+        return out
 
     def argmax_async(self, dtype: str, shard: torch.Tensor, stream=None) -> torch.Tensor:
         """max / argmax of any OrderedType over the sharded array.  32-bit

@@ -194,6 +194,16 @@ uint64_t f4s_hotpath_module(const f4s_hotpath* hotpath);
 int f4s_hotpath_sm_count(const f4s_hotpath* hotpath);
 /* CTAs per cluster of the full-array reductions (1..8, default 4). */
 int f4s_hotpath_set_reduce_cluster(f4s_hotpath* hotpath, int32_t cluster);
+/* Launch overlap of the device-resident full-array reductions
+ * (f4s_reduce_sum_f32 / _i32 / _argmax_f32, f4s_reduce_sum, f4s_reduce_argmax,
+ * f4s_reduce_sum_policy under Fast):
+ * when enabled, each is launched as a programmatic dependent of the kernel
+ * before it on the stream, so it starts reading its input while that kernel
+ * finishes and waits for it only before writing its workspace and output.
+ * Enable only when no kernel that writes a reduction's input is launched
+ * immediately before that reduction on the same stream.  Off by default.
+ * No counterpart in the reference (its launches are fully serialized). */
+int f4s_hotpath_set_launch_overlap(f4s_hotpath* hotpath, int32_t enable);
 
 /* Device-side waits never spin forever: a kernel that waits on a barrier
  * (the TMA-staged RMSNorm) gives up after a bounded number of polls,

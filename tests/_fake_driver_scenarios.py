@@ -17,7 +17,7 @@ FAKE = C.CDLL(sys.argv[2])
 class Launch(C.Structure):
     _fields_ = [("name", C.c_char * 64), ("grid", C.c_uint * 3), ("block", C.c_uint * 3), ("smem", C.c_uint),
                 ("cluster", C.c_int), ("cluster_dim", C.c_uint * 3), ("nparams", C.c_int),
-                ("params", (C.c_ubyte * 8) * 32), ("stream", C.c_ulonglong)]
+                ("params", (C.c_ubyte * 8) * 32), ("stream", C.c_ulonglong), ("programmatic", C.c_int)]
 
 
 FAKE.fake_last_launch.restype = C.POINTER(Launch)
@@ -171,9 +171,21 @@ def hotpath_dispatch():
     hp.reduce_into(f4s.REDUCE_SUM_F32, big, out, n=1 << 32)
     L = check("f4s_reduce_sum_f32", 37 * 8 * 4, block=512, cluster=4)
     assert (param(L, 1, 4), param(L, 2, 4)) == (0, 1)  # n = 2^32 split in two u32
+    assert L.programmatic == 0  # launch overlap is off by default
     hp.reduce_into(f4s.REDUCE_ARGMAX_F32, big, out, n=1000, index_base=(1 << 32) + 5, accumulate=True)
     L = check("f4s_reduce_argmax_f32", 4, block=512, cluster=4)
     assert (param(L, 5, 4), param(L, 6, 4), param(L, 7, 4)) == (5, 1, 1)
+    # with launch overlap the device-resident reductions are programmatic dependents
+    hp.set_launch_overlap(True)
+    hp.reduce_into(f4s.REDUCE_SUM_I32, big, out, n=1 << 20)
+    assert check("f4s_reduce_sum_i32", 32 * 4, block=512, cluster=4).programmatic == 1
+    hp.reduce_sum_into("bf16", big, out, n=1000)
+    assert last().programmatic == 1
+    hp.vector_add_f32(big, big, big, n=1 << 10)  # other operators never are
+    assert last().programmatic == 0
+    hp.set_launch_overlap(False)
+    hp.reduce_into(f4s.REDUCE_SUM_I32, big, out, n=1 << 20)
+    assert last().programmatic == 0
     # typed ReduceSum: kernel per input type, grid sized in 16-byte vectors
     for dtype, kernel in [("e4m3", "e4m3"), ("e5m2", "e5m2"), ("f16", "f16"), ("bf16", "bf16"), ("f64", "f64"),
                           ("u32", "i32"), ("i32", "i32"), ("f32", "f32")]:

@@ -47,6 +47,7 @@ typedef struct {
   int nparams;
   unsigned char params[32][8];
   unsigned long long stream;
+  int programmatic; /* CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION set */
 } Launch;
 
 static Launch last_launch;
@@ -258,6 +259,8 @@ static CUresult f_launch(const CUlaunchConfig* c, CUfunction f, void** params, v
   last_launch.smem = c->sharedMemBytes;
   last_launch.stream = (unsigned long long)(uintptr_t)c->hStream;
   for (unsigned i = 0; i < c->numAttrs; ++i) {
+    if (c->attrs[i].id == CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION)
+      last_launch.programmatic = c->attrs[i].value.programmaticStreamSerializationAllowed != 0;
     if (c->attrs[i].id == CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION) {
       last_launch.cluster = 1;
       last_launch.cluster_dim[0] = c->attrs[i].value.clusterDim.x;

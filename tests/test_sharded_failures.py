@@ -42,28 +42,6 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-class _OraclePartials:
-    """Stands in for the hot path on a CPU rank: writes the oracle's partial
-    of the shard into the reducer's partial tensor, as the kernel would."""
-
-    workspace_bytes = 0
-
-    def reduce_into(self, op, shard, out, n, stream, index_base, workspace):
-        import flight4s_b200 as f4s
-        from oracle import oracle as orc
-        x = np.ascontiguousarray(shard.numpy()[:n])
-        if op == f4s.REDUCE_SUM_F32:
-            out[0] = orc.sum_f32_exact(x)[0]
-        elif op == f4s.REDUCE_SUM_I32:
-            out[0] = int(orc.sum_i32(x))
-        elif op == f4s.REDUCE_ARGMAX_F32:
-            v, i = orc.argmax_f32(x)
-            out[0] = orc.argmax_packed_key(v, i + index_base) if i >= 0 else -(1 << 63)
-            out[1] = i + index_base if i >= 0 else -1
-        else:
-            raise ValueError(op)
-
-
 def _step(red, x, xi, monitor: bool):
     if monitor:
         red.begin_step()
@@ -82,13 +60,15 @@ def _finish(q, item):
 
 def _worker(rank: int, world: int, port: int, scenario: str, q, release):
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from _cpu_partials import OraclePartials
     from flight4s_b200 import sharded
     from oracle import oracle as orc
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     # the process group's own timeout is the last bound, well above the checks
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
     monitor = sharded.RankMonitor(timeout_s=MONITOR_TIMEOUT_S)
-    red = sharded.ShardedReducer(_OraclePartials(), torch.device("cpu"), N_TOTAL, monitor=monitor)
+    red = sharded.ShardedReducer(OraclePartials(), torch.device("cpu"), N_TOTAL, monitor=monitor)
     xa = orc.uniform_f32(N_TOTAL, seed=5)
     xia = orc.uniform_i32(N_TOTAL, seed=5, lo=-1000, hi=1000)
     x = torch.from_numpy(xa[red.offset:red.offset + red.count].copy())

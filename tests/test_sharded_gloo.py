@@ -179,3 +179,75 @@ def test_shard_bounds_cover_exactly():
             assert spans[0][0] == 0
             assert all(a[0] + a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert spans[-1][0] + spans[-1][1] == n
+
+
+def _batch_worker(rank: int, world: int, port: int, q):
+    """Batched steps (kernels back to back, all_reduces after the block,
+    partials alternating between two buffers), two batches in flight before
+    each wait, then an unbatched step."""
+    import sys
+    import torch
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.dirname(here))
+    from _cpu_partials import OraclePartials
+    from oracle import oracle as orc
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n = 50_021
+    red = sharded.ShardedReducer(OraclePartials(), torch.device("cpu"), n)
+
+    def shards(step):
+        lo, hi = red.offset, red.offset + red.count
+        return (torch.from_numpy(orc.uniform_f32(n, seed=100 + step)[lo:hi].copy()),
+                torch.from_numpy(orc.uniform_i32(n, seed=100 + step, lo=-1000, hi=1000)[lo:hi].copy()))
+
+    out = {}
+    for step in range(4):
+        x, xi = shards(step)
+        with red.batch():
+            red.sum_f32_async(x, stream=0)
+            red.argmax_f32_async(x, stream=0)
+            red.sum_i32_async(xi, stream=0)
+        bufs = (red.f64, red.i32, red.arg)  # this step's partials
+        if step % 2 == 0:
+            held = (step, bufs)  # read after the next batch, which writes the other buffers
+            continue
+        assert all(a is not b for a, b in zip(held[1], bufs))
+        red.wait_checked(30.0)
+        for s_, b in (held, (step, bufs)):
+            out[s_] = (float(b[0].item()), int(b[1].item()), int(b[2][0].item()))
+    x, xi = shards(4)
+    s4, i4 = red.sum_f32(x, stream=0), red.sum_i32(xi, stream=0)
+    red.argmax_f32_async(x, stream=0)
+    red.wait()
+    out[4] = (s4, i4, int(red.arg[0].item()))
+    q.put((rank, out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gloo_batched_steps_alternate_partials():
+    from oracle import oracle as orc
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n = 50_021
+    for step in range(5):
+        x = orc.uniform_f32(n, seed=100 + step)
+        xi = orc.uniform_i32(n, seed=100 + step, lo=-1000, hi=1000)
+        exact, abs_sum = orc.sum_f32_exact(x)
+        v, idx = orc.argmax_f32(x)
+        for rank in range(world):
+            got = results[rank][step]
+            assert abs(got[0] - exact) <= 1e-12 * abs_sum, (rank, step)
+            assert got[1] == orc.sum_i32(xi), (rank, step)
+            assert got[2] == orc.argmax_packed_key(v, idx), (rank, step)
