@@ -346,6 +346,13 @@ class ShardedReducer:
         all_reduces together when the block ends (see the class notes)."""
         if self._deferred is not None:
             raise RuntimeError("batches do not nest")
+        # The buffers this batch writes were last combined two batches ago:
+        # order the stream after those collectives here, before the first
+        # kernel, so nothing is queued between the batch's kernels.
+        with self._on(stream):
+            for op, idx in self._cur.items():
+                if (op, idx ^ 1) in self._pending:
+                    self._pending.release((op, idx ^ 1))
         self._deferred = []
         try:
             yield self

@@ -53,6 +53,22 @@ def main() -> None:
         typed.update({f"argmax_{k}": list(red.argmax(k, v))
                       for k, v in (("u32", xis.view(torch.int32)), ("f16", f16), ("f64", f64))})
         results.append({"sum_f32": s, "sum_i32": i, "argmax_packed": packed, "typed": typed})
+    # batched steps with launch overlap (two batches in flight, partials
+    # alternating between two buffers): the same results as the plain calls
+    hp.set_launch_overlap(True)
+    batched = []
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        held = []
+        for _ in range(2):
+            with red.batch(stream):
+                red.sum_f32_async(xs, stream)
+                red.argmax_f32_async(xs, stream)
+                red.sum_i32_async(xis, stream)
+            held.append((red.f64, red.i32, red.arg))
+        red.wait(stream)
+        batched += [[float(b[0].item()), int(b[1].item()), int(b[2][0].item())] for b in held]
+    hp.set_launch_overlap(False)
     # order-fixed sums over granule-aligned shards: the same bits as one GPU
     red_o = ShardedReducer(hp, dev, n_total, granule=ORDERED_GRANULE)
     xo = torch.empty(max(red_o.count, 1), dtype=torch.float32, device=dev)
@@ -67,7 +83,7 @@ def main() -> None:
     dist.barrier(device_ids=[local])
     if dist.get_rank() == 0:
         Path(out_path).write_text(json.dumps({"world": dist.get_world_size(), "results": results,
-                                              "ordered": ordered}))
+                                              "ordered": ordered, "batched": batched}))
     ctx.close()
     dist.destroy_process_group()
 

@@ -60,6 +60,10 @@ def test_two_gpu_sharded_reductions_match_oracle(tmp_path, n_total):
                            ("f64", x.astype(np.float64))):
             i, _ = orc.argmax_typed(dtype, arr)
             assert t[f"argmax_{dtype}"][1] == i, dtype
+    # batched steps with launch overlap: the same results as the plain calls
+    for r in got["results"]:
+        for b in got["batched"]:
+            assert b == [r["sum_f32"], r["sum_i32"], r["argmax_packed"]]
     # order-fixed sums: bit-identical to the single-array restatement
     want_f32, _ = orc.sum_ordered("f32", x)
     want_bf16, _ = orc.sum_ordered("bf16", orc.f32_to_bf16(x))
@@ -86,3 +90,21 @@ def test_two_gpu_argmax_past_32_bit_indices(tmp_path):
     for r in got["results"]:
         assert r["f32"] == [1000.0, (1 << 32) + 50]
         assert r["bf16"] == [1000.0, (1 << 32) + 50]
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_two_gpu_rank_leaving_between_steps(tmp_path):
+    """Rank 1 leaves after step 1 (announced, nothing in flight); rank 0
+    raises RankFailure on the host before launching step 2 and aborts its
+    communicator, within a second."""
+    out = tmp_path / "leave.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", str(HERE / "_sharded_leave_worker.py"), str(out)]
+    proc = subprocess.run(["timeout", "-k", "30", "180"] + cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    got = json.loads(out.read_text())
+    x = orc.uniform_f32(1 << 24, seed=5)
+    exact, abs_sum = orc.sum_f32_exact(x)
+    assert abs(got["first"] - exact) <= 1e-5 * abs_sum
+    assert got["outcome"] == "RankFailure" and got["elapsed"] < 1.0
