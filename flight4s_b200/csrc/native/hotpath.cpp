@@ -596,8 +596,9 @@ CUresult Hotpath::softmax_rows(CUstream stream, CUdeviceptr in, CUdeviceptr out,
   const int vpt = row_vectors_per_thread(cols, in, out);
   const std::string name = vpt ? "f4s_softmax_rows_bf16_v" + std::to_string(vpt) : "f4s_softmax_rows_bf16_any";
   const CUfunction fn = function(name);
-  // one CTA per row (measured best: no persistent tail)
-  const int grid = rows;
+  // two rows per CTA for rows of up to 8192 elements (VPT <= 4), one row per
+  // CTA for wider ones (no persistent tail either way)
+  const int grid = (vpt >= 1 && vpt <= 4) ? (rows + 1) / 2 : rows;
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
   ArgumentPack args;

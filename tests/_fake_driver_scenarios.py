@@ -149,10 +149,12 @@ def hotpath_dispatch():
         hp.vector_add(dtype, big, big, big, n=1 << 20)
         L = check(f"f4s_vector_add_{kernel}", (1 << 20) // per_cta)
         assert param(L, 3, 4) == 1 << 20
-    hp.softmax_rows_bf16(big, big, 32768, 8192)
-    check("f4s_softmax_rows_bf16_v4", 32768)
-    hp.softmax_rows_bf16(big, big, 10, 1000)
-    check("f4s_softmax_rows_bf16_v1", 10)
+    hp.softmax_rows_bf16(big, big, 32768, 8192)  # two rows per CTA
+    check("f4s_softmax_rows_bf16_v4", 16384)
+    hp.softmax_rows_bf16(big, big, 11, 1000)
+    check("f4s_softmax_rows_bf16_v1", 6)
+    hp.softmax_rows_bf16(big, big, 10, 8 * 2048)  # the widest register rows: one row per CTA
+    check("f4s_softmax_rows_bf16_v8", 10)
     hp.softmax_rows_bf16(big, big, 10, 1001)
     check("f4s_softmax_rows_bf16_any", 10)
     hp.rmsnorm_rows_bf16(big, big, big, 32768, 8192)
