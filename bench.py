@@ -734,7 +734,8 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
     ws = torch.zeros(hp.block_reduce_workspace_bytes(n), dtype=torch.uint8, device=dev)
     # A 4 MiB block sum runs for a few microseconds, less than one host-side
     # launch through Python, so it is timed as CUDA-graph replays of
-    # back-to-back launches (device time per launch).
+    # back-to-back calls (device time per call: the tiles kernel and its
+    # one-CTA upper pass).
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def graph_ms(body, count):
@@ -749,17 +750,20 @@ def kernel_table(ctx, hp, dev, peak) -> dict:
                     body()
         g.replay()
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        g.replay()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / count
+        times = []
+        for _ in range(7):  # median of 7 replays
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) / count)
+        return sorted(times)[3]
 
     bs = lambda: hp.block_reduce_sum_f32_into(x, parts, o, ws, stream=torch.cuda.current_stream())  # noqa: E731
-    row("block_reduce_sum_f32 n=2^20 hot-L2", 4 * n + 4 * (n // 256), n, graph_ms(bs, 100), timing="cuda graph")
+    row("block_reduce_sum_f32 n=2^20 hot-L2", 4 * n + 4 * (n // 256), n, graph_ms(bs, 100), timing="cuda graph, median of 7 replays")
     flushed = graph_ms(lambda: (flush.zero_(), bs()), 50) - graph_ms(lambda: flush.zero_(), 50)
-    row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, flushed, timing="cuda graph")
+    row("block_reduce_sum_f32 n=2^20 L2-flushed", 4 * n + 4 * (n // 256), n, flushed, timing="cuda graph, median of 7 replays")
     del flush
     torch.cuda.empty_cache()  # next section on freshly allocated buffers
 

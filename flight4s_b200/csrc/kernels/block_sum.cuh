@@ -24,12 +24,16 @@
 //   * the last cluster to finish (atomic ticket, no waiting) computes the
 //     remaining levels from the level-2 partials in global workspace.
 //
-// Arrays of up to kBlockSumCtaMaxTiles tiles (2^23 elements) take a second
-// kernel with the same tree and no cluster: every CTA stores its 32 tile
-// partials and takes a ticket, and the last CTA computes levels 2+ straight
-// from the tile partials.  At these sizes one extra L2 read of the tile
-// partials by one CTA is cheaper than a barrier across an 8-CTA cluster
-// (n = 2^20: 3.3 us against 3.6-4.3 us, L2-flushed 4.2 against 4.8-5.0).
+// Arrays of up to kBlockSumSmallMaxTiles tiles (2^23 elements) take two
+// launches instead and no workspace: a tiles kernel (level 1 only) and a
+// one-CTA upper pass (levels 2+) launched as its programmatic dependent, so
+// it is already resident when the last tile partial lands.  Same tree, same
+// bits.  Measured at n = 2^20 by CUDA-graph replay on B200: empty launch of
+// the level-1 shape 0.59 us, level 1 alone 1.72 us, level 1 + the ticket of
+// the former one-launch form 2.48 us, that form complete 3.31-3.34 us
+// (L2-flushed 4.74-4.84), this pair 3.17-3.21 us (flushed 4.41-4.44).
+// Slots polled by the last or a designated CTA instead of a ticket, and a
+// one-warp upper pass, measured slower (3.46-4.48 us).
 #pragma once
 
 #include <cooperative_groups.h>
@@ -44,9 +48,10 @@ constexpr int kBlockSumWarps = kBlockSumThreads / kWarp;    // 32 tiles per CTA
 constexpr int kBlockSumCluster = 8;                         // 256 tiles per cluster
 // Workspace layout: [0,4) ticket; level-2 partials from byte 256.
 constexpr int kBlockSumLevel2Offset = 256;
-// Largest tile count of the cluster-free kernel: its last CTA holds the
+// Largest tile count of the two-launch form: its upper pass holds the
 // level-2 nodes (one per 256 tiles) in a 256-entry shared array.
-constexpr unsigned kBlockSumCtaMaxTiles = 128u * kTile;
+constexpr unsigned kBlockSumSmallMaxTiles = 128u * kTile;
+constexpr int kBlockSumUpperThreads = 512;
 
 // One 256-ary tree node in the reference order; `v[k]` = element
 // (lane + 32k) of the node's 256 inputs.  Returns the node value in lane 0.
@@ -173,23 +178,20 @@ f4s_block_reduce_sum_f32(const float* __restrict__ in, int n, float* __restrict_
   }
 }
 
-// (in, n, partials[ceil(n/256)], out[1], workspace) for n <= 2^23.  Launch
-// with blockDim 1024, no cluster, grid = max(1, ceil(n / 8192)).  Same tree
-// and bits as f4s_block_reduce_sum_f32; workspace: the ticket at [0,4).
+// Arrays of up to 2^23 elements: two launches, no workspace.
+//
+// f4s_block_sum_tiles_f32 (in, n, partials[ceil(n/256)]): level 1, one tile
+// per warp.  Launch with blockDim 1024, grid = max(1, ceil(n / 8192)).
+// Every CTA first lets the dependent launch start, so the one-CTA upper pass
+// below is resident and waiting before the last tile is summed.
 extern "C" __global__ void __launch_bounds__(f4s::kBlockSumThreads)
-f4s_block_reduce_sum_f32_cta(const float* __restrict__ in, int n, float* __restrict__ partials,
-                             float* __restrict__ out, unsigned char* __restrict__ workspace) {
+f4s_block_sum_tiles_f32(const float* __restrict__ in, int n, float* __restrict__ partials) {
   using namespace f4s;
-  __shared__ float level_a[kTile];
-  __shared__ float level_b[kTile];
-  __shared__ int is_last;
-
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x / kWarp;
   const int lane = threadIdx.x % kWarp;
   const unsigned tiles = (static_cast<unsigned>(n) + kTile - 1) / kTile;
   const unsigned tile = blockIdx.x * kBlockSumWarps + warp;
-
-  // level 1: one tile per warp (zero padded past n)
   float v[8];
   const size_t tile_base = static_cast<size_t>(tile) * kTile;
 #pragma unroll
@@ -199,40 +201,40 @@ f4s_block_reduce_sum_f32_cta(const float* __restrict__ in, int n, float* __restr
   }
   const float tile_sum = tree256(v);
   if (lane == 0 && tile < tiles) partials[tile] = tile_sum;
+}
 
-  // The barrier makes the CTA's partial stores precede thread 0's
-  // acquire-release ticket, which publishes them at GPU scope; the last CTA's
-  // ticket acquires every other CTA's.
-  __syncthreads();
-  unsigned int* ticket = reinterpret_cast<unsigned int*>(workspace);
-  if (threadIdx.x == 0) is_last = (ticket_acq_rel(ticket) == gridDim.x - 1) ? 1 : 0;
-  __syncthreads();
-  if (!is_last) return;
-
-  // levels 2+ on the last CTA: the first from the tile partials in L2
-  unsigned count = tiles;
+// f4s_block_sum_upper_f32 (partials, n, out): levels 2+ from the tile
+// partials, one CTA of kBlockSumUpperThreads.  Launched right after the tiles
+// kernel on the same stream as its programmatic dependent: griddepcontrol.wait
+// returns once that grid has completed and its partial stores are visible
+// (for an ordinary launch it returns at once, the stream having already
+// ordered the two).  Nothing is read before the wait.
+extern "C" __global__ void __launch_bounds__(f4s::kBlockSumUpperThreads)
+f4s_block_sum_upper_f32(const float* __restrict__ partials, int n, float* __restrict__ out) {
+  using namespace f4s;
+  __shared__ float level_a[kTile];
+  __shared__ float level_b[kTile];
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  constexpr int kWarps = kBlockSumUpperThreads / kWarp;
+  unsigned count = (static_cast<unsigned>(n) + kTile - 1) / kTile;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count <= 1) {  // one tile (or none) is already the final value
-    if (threadIdx.x == 0) {
-      out[0] = (count == 1) ? __ldcg(partials) : 0.0f;
-      *ticket = 0u;
-    }
+    if (threadIdx.x == 0) out[0] = (count == 1) ? __ldcg(partials) : 0.0f;
     return;
   }
-  tree_level(partials, count, level_a, warp, lane, kBlockSumWarps, true);
+  tree_level(partials, count, level_a, warp, lane, kWarps, true);
   count = (count + kTile - 1) / kTile;
   float* cur = level_a;
   float* nxt = level_b;
   __syncthreads();
   while (count > 1) {
-    tree_level(cur, count, nxt, warp, lane, kBlockSumWarps, false);
+    tree_level(cur, count, nxt, warp, lane, kWarps, false);
     count = (count + kTile - 1) / kTile;
     float* tmp = cur;
     cur = nxt;
     nxt = tmp;
     __syncthreads();
   }
-  if (threadIdx.x == 0) {
-    out[0] = cur[0];
-    *ticket = 0u;
-  }
+  if (threadIdx.x == 0) out[0] = cur[0];
 }

@@ -29,8 +29,9 @@ constexpr int kBlockSumCluster = 8;
 constexpr std::int64_t kBlockSumElemsPerCluster = 256LL * 256LL;
 constexpr std::int64_t kBlockSumWarps = kBlockSumThreads / 32;
 // Arrays of at most this many 256-element tiles (2^23 elements) take the
-// cluster-free kernel (csrc/kernels/block_sum.cuh: kBlockSumCtaMaxTiles).
-constexpr std::int64_t kBlockSumCtaMaxTiles = 128LL * 256LL;
+// two-launch form (csrc/kernels/block_sum.cuh: kBlockSumSmallMaxTiles).
+constexpr std::int64_t kBlockSumSmallMaxTiles = 128LL * 256LL;
+constexpr int kBlockSumUpperThreads = 512;
 constexpr int kAddBlock = 256;
 constexpr int kRowBlock = 256;
 constexpr int kFp8Threads = 256;
@@ -522,14 +523,22 @@ CUresult Hotpath::block_sum_f32(CUstream stream, CUdeviceptr in, std::int32_t n,
                                 " bytes, need " + std::to_string(block_sum_workspace_bytes(n)));
   Current cur(context_);
   if (cur.result() != CUDA_SUCCESS) return cur.result();
+  const std::int64_t tiles = (static_cast<std::int64_t>(n) + 255) / 256;
+  if (tiles <= kBlockSumSmallMaxTiles) {
+    // small arrays: the tiles kernel, then the one-CTA upper pass as its
+    // programmatic dependent (same tree, same bits; the workspace is unused)
+    const int ctas = static_cast<int>(std::max<std::int64_t>(1, (tiles + kBlockSumWarps - 1) / kBlockSumWarps));
+    ArgumentPack tiles_args;
+    tiles_args.ptr(in).i32(n).ptr(partials);
+    const CUresult r = launch(function("f4s_block_sum_tiles_f32"), stream, ctas, kBlockSumThreads, 0, tiles_args);
+    if (r != CUDA_SUCCESS) return cur.finish(r);
+    ArgumentPack upper_args;
+    upper_args.ptr(partials).i32(n).ptr(out);
+    return cur.finish(launch(function("f4s_block_sum_upper_f32"), stream, 1, kBlockSumUpperThreads, 0, upper_args,
+                             true));
+  }
   ArgumentPack args;
   args.ptr(in).i32(n).ptr(partials).ptr(out).ptr(workspace);
-  const std::int64_t tiles = (static_cast<std::int64_t>(n) + 255) / 256;
-  if (tiles <= kBlockSumCtaMaxTiles) {
-    // small arrays: no cluster, every CTA takes a ticket (same tree, same bits)
-    const int ctas = static_cast<int>(std::max<std::int64_t>(1, (tiles + kBlockSumWarps - 1) / kBlockSumWarps));
-    return cur.finish(launch(function("f4s_block_reduce_sum_f32_cta"), stream, ctas, kBlockSumThreads, 0, args));
-  }
   const int clusters = static_cast<int>(std::max<std::int64_t>(1, (static_cast<std::int64_t>(n) + kBlockSumElemsPerCluster - 1) / kBlockSumElemsPerCluster));
   return cur.finish(launch(function("f4s_block_reduce_sum_f32"), stream, clusters * kBlockSumCluster,
                            kBlockSumThreads, kBlockSumCluster, args));

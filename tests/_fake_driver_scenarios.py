@@ -254,11 +254,16 @@ def hotpath_dispatch():
     assert count() == before
     parts = ctx.allocate("f32", 4096)
     ws = ctx.allocate("u8", hp.block_reduce_workspace_bytes(1 << 20))
-    # up to 2^23 elements: the cluster-free kernel, one 1024-thread CTA per 32 tiles
-    hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1 << 20)
-    check("f4s_block_reduce_sum_f32_cta", 128, block=1024)
-    hp.block_reduce_sum_f32_into(big, parts, out, ws, n=1)
-    check("f4s_block_reduce_sum_f32_cta", 1, block=1024)
+    # up to 2^23 elements: the tiles kernel (one 1024-thread CTA per 32 tiles),
+    # then the one-CTA upper pass launched as its programmatic dependent
+    FAKE.fake_launch_at.restype = C.POINTER(Launch)
+    for n, ctas in [(1 << 20, 128), (1, 1)]:
+        before = count()
+        hp.block_reduce_sum_f32_into(big, parts, out, ws, n=n)
+        L = [FAKE.fake_launch_at(i).contents for i in range(before, count())]
+        assert [x.name.decode() for x in L] == ["f4s_block_sum_tiles_f32", "f4s_block_sum_upper_f32"]
+        assert (L[0].grid[0], L[0].block[0], L[1].grid[0], L[1].block[0]) == (ctas, 1024, 1, 512)
+        assert (L[0].programmatic, L[1].programmatic) == (0, 1)
     # above: clusters of 8 CTAs, one per 65536 elements
     n_big = (1 << 23) + 1
     ws_big = ctx.allocate("u8", hp.block_reduce_workspace_bytes(n_big))

@@ -72,7 +72,8 @@ static const Signature signatures[] = {
     {"f4s_reduce_sum_i32", 8, {8, 4, 4, 8, 8, 4, 4, 4}},
     {"f4s_reduce_argmax_f32", 8, {8, 4, 4, 8, 8, 4, 4, 4}},
     {"f4s_block_reduce_sum_f32", 5, {8, 4, 8, 8, 8}},
-    {"f4s_block_reduce_sum_f32_cta", 5, {8, 4, 8, 8, 8}},
+    {"f4s_block_sum_tiles_f32", 3, {8, 4, 8}},
+    {"f4s_block_sum_upper_f32", 3, {8, 4, 8}},
     {"f4s_softmax_rows_bf16_v4", 4, {8, 8, 4, 4}},
     {"f4s_softmax_rows_bf16_any", 4, {8, 8, 4, 4}},
     {"f4s_rmsnorm_rows_bf16_tma", 6, {8, 8, 8, 4, 4, 4}},
