@@ -1,8 +1,9 @@
 """torchrun worker for tests/test_gpu_sharded.py: two ranks run one sharded
 step on their GPUs; then rank 1 leaves between steps (announced through
 the rank monitor, with nothing of its own in flight) and rank 0 must raise
-RankFailure on the host before launching anything of step 2, abort its
-communicator and report how long that took (JSON to argv[1])."""
+RankFailure on the host before launching anything of step 2 and abort its
+communicator; it reports how long the detection and the abort each took
+(JSON to argv[1])."""
 import json
 import os
 import sys
@@ -39,14 +40,17 @@ def main() -> None:
         dist.destroy_process_group()
         return
     t0 = time.monotonic()
+    t_abort = None
     try:
         red.begin_step()
         outcome = "no error"
     except RankFailure:
         outcome = "RankFailure"
+        t_abort = time.monotonic()
         red.abort()
-    elapsed = time.monotonic() - t0
-    Path(out_path).write_text(json.dumps({"first": first, "outcome": outcome, "elapsed": elapsed}))
+    elapsed = (t_abort if t_abort is not None else time.monotonic()) - t0
+    abort_s = time.monotonic() - t_abort if t_abort is not None else None
+    Path(out_path).write_text(json.dumps({"first": first, "outcome": outcome, "elapsed": elapsed, "abort_s": abort_s}))
     ctx.close()
 
 
