@@ -259,7 +259,12 @@ def main() -> None:
         # NCCL may print a version banner on stdout while the communicator
         # comes up; keep stdout for the one JSON line.
         with _stdout_to_stderr():
-            dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300))
+            # NCCL on a high-priority stream: the step's small all_reduces are
+            # scheduled ahead of the next step's reduction CTAs (measured
+            # 2-3 us less exposed collective time per step at 2^29 per rank)
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+            dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300), pg_options=opts)
             dist.barrier(device_ids=[local])
             torch.cuda.synchronize()
     ctx = f4s.CudaContext.open(local)
