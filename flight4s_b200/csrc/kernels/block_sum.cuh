@@ -31,7 +31,7 @@
 // bits.  Measured at n = 2^20 by CUDA-graph replay on B200: empty launch of
 // the level-1 shape 0.59 us, level 1 alone 1.72 us, level 1 + the ticket of
 // the former one-launch form 2.48 us, that form complete 3.31-3.34 us
-// (L2-flushed 4.74-4.84), this pair 3.17-3.21 us (flushed 4.41-4.44).
+// (L2-flushed 4.74-4.84), this pair 3.08-3.21 us (flushed 4.40-4.44).
 // Slots polled by the last or a designated CTA instead of a ticket, and a
 // one-warp upper pass, measured slower (3.46-4.48 us).
 #pragma once
@@ -213,28 +213,41 @@ extern "C" __global__ void __launch_bounds__(f4s::kBlockSumUpperThreads)
 f4s_block_sum_upper_f32(const float* __restrict__ partials, int n, float* __restrict__ out) {
   using namespace f4s;
   __shared__ float level_a[kTile];
-  __shared__ float level_b[kTile];
   const int warp = threadIdx.x / kWarp;
   const int lane = threadIdx.x % kWarp;
   constexpr int kWarps = kBlockSumUpperThreads / kWarp;
-  unsigned count = (static_cast<unsigned>(n) + kTile - 1) / kTile;
+  const unsigned count = (static_cast<unsigned>(n) + kTile - 1) / kTile;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count <= 1) {  // one tile (or none) is already the final value
     if (threadIdx.x == 0) out[0] = (count == 1) ? __ldcg(partials) : 0.0f;
     return;
   }
-  tree_level(partials, count, level_a, warp, lane, kWarps, true);
-  count = (count + kTile - 1) / kTile;
-  float* cur = level_a;
-  float* nxt = level_b;
-  __syncthreads();
-  while (count > 1) {
-    tree_level(cur, count, nxt, warp, lane, kWarps, false);
-    count = (count + kTile - 1) / kTile;
-    float* tmp = cur;
-    cur = nxt;
-    nxt = tmp;
-    __syncthreads();
+  // level 2: one node per warp, from the tile partials in L2
+  const unsigned nodes = (count + kTile - 1) / kTile;  // <= 128 for n <= 2^23
+  if (nodes == 1) {  // warp 0 holds the final value: no barrier needed
+    if (warp == 0) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const unsigned i = lane + 32 * k;
+        v[k] = (i < count) ? __ldcg(partials + i) : 0.0f;
+      }
+      const float r = tree256(v);
+      if (lane == 0) out[0] = r;
+    }
+    return;
   }
-  if (threadIdx.x == 0) out[0] = cur[0];
+  tree_level(partials, count, level_a, warp, lane, kWarps, true);
+  __syncthreads();
+  // level 3 (the last one: at most 128 nodes) on warp 0
+  if (warp == 0) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const unsigned i = lane + 32 * k;
+      v[k] = (i < nodes) ? level_a[i] : 0.0f;
+    }
+    const float r = tree256(v);
+    if (lane == 0) out[0] = r;
+  }
 }
