@@ -22,8 +22,10 @@
 // used in the context it was looked up in.  That first call per context may
 // load this file's device code, which a stream capture cannot record: it is
 // rejected with F4S_STATUS_INVALID_ARGUMENT while `stream` is capturing, so
-// make it before any capture.  The block-sum kernel is the same one the
-// regular entry point launches; only the workspace differs.
+// make it before any capture.  The block-sum kernels are the same ones the
+// regular entry point launches; only the workspace differs (arrays of up to
+// 2^23 elements take the two-launch form, which reads no workspace, so only
+// larger arrays use the array's ticket and partials).
 //
 // Limits and sharing: the workspace holds 256 bytes of header plus one
 // 4-byte partial per 65536-element cluster, so n may be at most
