@@ -111,7 +111,7 @@ class _SecondContext:
 
 
 def test_noalloc_in_a_second_context_of_the_gpu(ctx, hp):
-    n = (1 << 20) + 77
+    n = (1 << 23) + 77  # above 2^23 the kernel keeps its ticket and partials in the static workspace
     tiles = (n + 255) // 256
     x = orc.uniform_f32(n, seed=0xC0DE)
     dx = ctx.allocate("f32", n)
