@@ -54,3 +54,35 @@ def test_repeated_launches_reuse_workspace(ctx, hp):
         hp.block_reduce_sum_f32_into(dx, parts, out, ws)
     ctx.synchronize()
     assert np.float32(out.copy_to_array()[0]) == np.float32(ref)
+
+
+@pytest.mark.parametrize("n", [(1 << 20) + 77, (1 << 23) + 5])
+def test_captured_in_a_cuda_graph(hp, torch_dev, n):
+    """Captured into a CUDA graph (up to 2^23 elements: the tiles kernel and
+    its programmatic dependent become two graph nodes), then replayed with a
+    kernel writing the input before each replay: every replay gives the
+    oracle's bits for the input it saw."""
+    import torch
+    x = torch.empty(n, dtype=torch.float32, device=torch_dev)
+    parts = torch.empty((n + 255) // 256, dtype=torch.float32, device=torch_dev)
+    out = torch.empty(1, dtype=torch.float32, device=torch_dev)
+    ws = torch.zeros(hp.block_reduce_workspace_bytes(n), dtype=torch.uint8, device=torch_dev)
+    src = [torch.from_numpy(orc.uniform_f32(n, seed=s)).to(torch_dev) for s in (11, 12)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        x.copy_(src[0])
+        hp.block_reduce_sum_f32_into(x, parts, out, ws, stream=side)  # warm-up outside the capture
+        side.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            hp.block_reduce_sum_f32_into(x, parts, out, ws, stream=side)
+    torch.cuda.synchronize()
+    for s, xs in zip((11, 12, 11), (src[0], src[1], src[0])):
+        x.copy_(xs)  # a kernel on the current stream, ordered before the replay
+        g.replay()
+        torch.cuda.synchronize()
+        ref_total, ref_parts = orc.block_tree_sum_f32(orc.uniform_f32(n, seed=s))
+        assert np.float32(out.item()).view(np.uint32) == np.float32(ref_total).view(np.uint32)
+        assert np.array_equal(parts.cpu().numpy().view(np.uint32), ref_parts.view(np.uint32))
+    del g
