@@ -369,7 +369,13 @@ int f4s_convert(f4s_hotpath* hotpath, uint64_t stream, int32_t from_type, int32_
  * extended to n elements: partials[t] = fp32 tree sum of tile t (256
  * elements, zero padded, the reference's stride order 128..1), then the same
  * tree over runs of 256 partials until one value remains in out[0].
- * Bit-identical to the reference kernel applied level by level. */
+ * Bit-identical to the reference kernel applied level by level.
+ * Asynchronous on `stream`: up to 2^23 elements two launches (the tile
+ * pass, then a one-CTA pass over the partials launched as its programmatic
+ * dependent; the workspace is not touched), above that one clustered launch
+ * that keeps a ticket and per-cluster partials in the workspace (zeroed once
+ * by the caller; the kernel leaves it zeroed).  Calls sharing a workspace
+ * must not overlap on the GPU. */
 uint64_t f4s_block_reduce_workspace_bytes(int32_t n);
 int f4s_block_reduce_sum_f32(f4s_hotpath* hotpath, uint64_t stream, uint64_t in, int32_t n, uint64_t partials,
                              uint64_t out, uint64_t workspace, uint64_t workspace_bytes);
