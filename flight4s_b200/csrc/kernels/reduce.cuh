@@ -94,6 +94,7 @@ struct SumF64PartialBase {
     double acc = 0.0;
   };
   static __device__ __forceinline__ Partial finish(Thread& t, uint64_t) { return t.acc; }
+  static __device__ __forceinline__ void before_body(Thread&, uint64_t) {}
   static __device__ __forceinline__ Partial identity() { return 0.0; }
   static __device__ __forceinline__ Partial merge(Partial a, Partial b) { return a + b; }
   static __device__ __forceinline__ Partial warp_merge(Partial v) { return warp_sum_f64(v); }
@@ -230,6 +231,7 @@ struct SumWrap32Op {
     t.acc += static_cast<uint32_t>(bits);
   }
   static __device__ __forceinline__ Partial finish(Thread& t, uint64_t) { return static_cast<int32_t>(t.acc); }
+  static __device__ __forceinline__ void before_body(Thread&, uint64_t) {}
   static __device__ __forceinline__ Partial identity() { return 0; }
   static __device__ __forceinline__ Partial merge(Partial a, Partial b) {
     return static_cast<int32_t>(static_cast<uint32_t>(a) + static_cast<uint32_t>(b));
@@ -361,6 +363,12 @@ struct ArgmaxOp {
   static __device__ __forceinline__ void scalar(Thread& t, uint64_t bits, uint64_t index) {
     argmax_merge(t.s, ArgmaxPartial{static_cast<int64_t>(K::key(bits)), static_cast<int64_t>(index)});
   }
+  // Before the body: the lane's lowest-index vector, if it reads any, is
+  // the candidate until a vector with a larger key than the smallest one
+  // turns up (the strict '>' against the initial key never fires for a
+  // lane that sees only the smallest key, e.g. an i32 array of INT32_MIN;
+  // its answer is then the first element of its first vector).
+  static __device__ __forceinline__ void before_body(Thread& t, uint64_t first) { t.best_vec = first; }
   static __device__ __forceinline__ Partial finish(Thread& t, uint64_t head) {
     ArgmaxPartial p = t.s;
     if (t.best_vec != UINT64_MAX) {
@@ -368,6 +376,7 @@ struct ArgmaxOp {
 #pragma unroll
       for (int j = kPerVec - 2; j >= 0; --j)
         if (K::key(vector_element<kElemBytes>(t.best, j)) == t.vkey) lane = j;
+      if (t.vkey == kKeyMin) lane = 0;  // never updated: every key seen was the smallest
       argmax_merge(p, ArgmaxPartial{static_cast<int64_t>(t.vkey),
                                     static_cast<int64_t>(head + kPerVec * t.best_vec + lane)});
     }
@@ -480,6 +489,11 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
   const uint64_t nwarps = nthreads / kWarp;
   const uint64_t full_tiles = nvec / (kWarp * kUnroll);
   uint64_t tile = tid / kWarp;
+  {
+    // the lowest-index vector this lane reads, if any
+    const uint64_t first = tile * (kWarp * kUnroll) + tile_lane;
+    Op::before_body(t, (tile <= full_tiles && first < nvec) ? first : UINT64_MAX);
+  }
   for (; tile < full_tiles; tile += nwarps) {
     const uint64_t base = tile * (kWarp * kUnroll) + tile_lane;
     uint4 v[kUnroll];

@@ -139,3 +139,22 @@ def test_full_size_against_torch(ctx, hp, torch_dev):
         assert value == x[want].item(), dtype
         del x
         torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("misalign", [0, 1])
+@pytest.mark.parametrize("n", [1, 7, 64, 4097, 1_000_003])
+@pytest.mark.parametrize("dtype", ["i32", "u32", "f32", "f64"])
+def test_every_element_holds_the_smallest_key(ctx, hp, dtype, n, misalign):
+    """An array whose every element has the smallest order key of its type
+    (i32 INT32_MIN, u32 0, f32 / f64 the negative NaN with every payload bit
+    set): the maximum is that key and the first index wins."""
+    storage = orc.CONVERT_STORAGE[dtype]
+    smallest = {"i32": np.array(-2**31, np.int64).astype(np.int32), "u32": np.uint32(0),
+                "f32": np.array(0xFFFFFFFF, np.uint32).view(np.float32),
+                "f64": np.array(0xFFFFFFFFFFFFFFFF, np.uint64).view(np.float64)}[dtype]
+    x = np.full(n, smallest, dtype=storage)
+    buf, addr = _upload(ctx, dtype, x, misalign)
+    got = _record(ctx, hp, dtype, addr, n)
+    assert got == orc.argmax_record(dtype, x)
+    assert got[1] == 0
+    buf.close()
