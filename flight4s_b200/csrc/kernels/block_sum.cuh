@@ -12,7 +12,8 @@
 // so the result is bit-identical to running the reference kernel level by
 // level.
 //
-// B200 mapping (one launch, no shared-memory barriers inside a tile):
+// B200 mapping (no shared-memory barriers inside a tile; for arrays above
+// 2^23 elements one clustered launch):
 //   * one warp owns one tile: lane l holds x[l + 32k], k = 0..7, which are
 //     eight coalesced 128-byte rows.  Strides 128/64/32 of the reference are
 //     register adds between those eight values, strides 16..1 are
