@@ -316,13 +316,14 @@ __device__ __forceinline__ uint64_t vector_element(const uint4& v, int j) {
 //            index) pair, valid while index < 2^32; for f64: the 64-bit key
 //            itself; INT64_MIN for an empty input;
 //   out[1] = the index as a signed 64-bit integer, -1 for an empty input.
-template <class K>
+template <class K, int U = 4>
 struct ArgmaxOp {
   static constexpr int kElemBytes = K::kBytes;
   static constexpr int kPerVec = 16 / K::kBytes;
-  // 4 vectors in flight per lane (f32: 39 registers, 3 CTAs per SM; +5% at
-  // 2^29 elements, +2% at 2^32 against 8 vectors at 2 CTAs per SM)
-  static constexpr int kUnroll = 4;
+  // U vectors in flight per lane: 4 where 3 CTAs per SM fit the registers
+  // (f32: 40 registers; +5% at 2^29 elements, +2% at 2^32 against 8 vectors
+  // at 2 CTAs per SM), 8 for the keys that hold 2 CTAs per SM
+  static constexpr int kUnroll = U;
   using Key = typename K::Key;
   using Partial = ArgmaxPartial;
   static constexpr Key kKeyMin = sizeof(Key) == 8 ? static_cast<Key>(INT64_MIN) : static_cast<Key>(INT32_MIN);
@@ -593,18 +594,18 @@ F4S_REDUCE_KERNEL(f4s_reduce_sum_f32, f4s::SumF32Op)
 F4S_REDUCE_KERNEL(f4s_reduce_sum_i32, f4s::SumWrap32Op)
 // max / argmax over every OrderedType.  MIN_CTAS: 3 per SM where that
 // fits in registers without spilling (f32, 16-bit), else 2.
-#define F4S_ARGMAX_KERNEL(NAME, KEY, MIN_CTAS)                                                         \
+#define F4S_ARGMAX_KERNEL(NAME, KEY, MIN_CTAS, UNROLL)                                                 \
   extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, MIN_CTAS)                             \
       NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace,           \
            uint32_t base_lo, uint32_t base_hi, int accumulate) {                                        \
-    f4s::reduce_full<f4s::ArgmaxOp<f4s::KEY>>(in, f4s::join_u64(n_lo, n_hi), out, workspace,            \
-                                              f4s::join_u64(base_lo, base_hi), accumulate);             \
+    f4s::reduce_full<f4s::ArgmaxOp<f4s::KEY, UNROLL>>(in, f4s::join_u64(n_lo, n_hi), out, workspace,    \
+                                                      f4s::join_u64(base_lo, base_hi), accumulate);     \
   }
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f32, ArgmaxKeyF32, 3)
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_i32, ArgmaxKeyI32, 2)
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_u32, ArgmaxKeyU32, 2)
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 3)  // f16 and bf16
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f32, ArgmaxKeyF32, 3, 4)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_i32, ArgmaxKeyI32, 2, 8)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_u32, ArgmaxKeyU32, 2, 8)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 3, 4)  // f16 and bf16
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2, 4)
 #undef F4S_ARGMAX_KERNEL
 // the other AccumulatorType inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
 // accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2

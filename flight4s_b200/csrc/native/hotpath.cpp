@@ -290,27 +290,34 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
 namespace {
 
 // 16-byte vectors per lane per step of each fast kernel (its Op::kUnroll in
-// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums, 4 for the rest.
+// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums and the i32 / u32 argmax,
+// 4 for the rest.
 int reduce_step_vectors(ReduceOp op) {
   switch (op) {
     case ReduceOp::kSumF16:
     case ReduceOp::kSumBf16:
     case ReduceOp::kSumF64:
     case ReduceOp::kSumE4m3:
-    case ReduceOp::kSumE5m2: return kReduceUnroll;
+    case ReduceOp::kSumE5m2:
+    case ReduceOp::kArgmaxI32:
+    case ReduceOp::kArgmaxU32: return kReduceUnroll;
     default: return kShortStepUnroll;
   }
 }
 
 // Waves of co-resident clusters in one launch: kReduceWaves, doubled for the
-// f64 and FP8 sums, whose kernels hold two CTAs per SM (~4544 CTAs either
-// way; measured +2-6 % over 8 waves at 2 and 8 GiB).  Every choice stays
-// within reduce_workspace_bytes(): at most 4 CTAs per SM x kReduceWaves.
+// kernels that hold two CTAs per SM with 8-vector steps — the f64 and FP8
+// sums and the i32 / u32 argmax (~4544 CTAs either way; measured +2-6 % for
+// the sums and +4 % for the argmax at 2 and 8 GiB over 8 waves of 4-vector
+// steps).  Every choice stays within reduce_workspace_bytes(): at most 4
+// CTAs per SM x kReduceWaves.
 int reduce_waves(ReduceOp op) {
   switch (op) {
     case ReduceOp::kSumF64:
     case ReduceOp::kSumE4m3:
-    case ReduceOp::kSumE5m2: return 2 * kReduceWaves;
+    case ReduceOp::kSumE5m2:
+    case ReduceOp::kArgmaxI32:
+    case ReduceOp::kArgmaxU32: return 2 * kReduceWaves;
     default: return kReduceWaves;
   }
 }
