@@ -320,9 +320,10 @@ template <class K, int U = 4>
 struct ArgmaxOp {
   static constexpr int kElemBytes = K::kBytes;
   static constexpr int kPerVec = 16 / K::kBytes;
-  // U vectors in flight per lane: 4 where 3 CTAs per SM fit the registers
-  // (f32: 40 registers; +5% at 2^29 elements, +2% at 2^32 against 8 vectors
-  // at 2 CTAs per SM), 8 for the keys that hold 2 CTAs per SM
+  // U vectors in flight per lane at 2 CTAs per SM, launched in 16 waves:
+  // 8 (6 for f64's 64-bit keys).  A/B on B200 against 4 vectors at 3 CTAs
+  // per SM in 8 waves: f32 +1.2 % at 16 GiB, +0.5 % at 2 GiB; f16 +3 %,
+  // i32 / u32 +4 %, f64 +2.4 % at 8 GiB.
   static constexpr int kUnroll = U;
   using Key = typename K::Key;
   using Partial = ArgmaxPartial;
@@ -601,11 +602,11 @@ F4S_REDUCE_KERNEL(f4s_reduce_sum_i32, f4s::SumWrap32Op)
     f4s::reduce_full<f4s::ArgmaxOp<f4s::KEY, UNROLL>>(in, f4s::join_u64(n_lo, n_hi), out, workspace,    \
                                                       f4s::join_u64(base_lo, base_hi), accumulate);     \
   }
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f32, ArgmaxKeyF32, 3, 4)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f32, ArgmaxKeyF32, 2, 8)
 F4S_ARGMAX_KERNEL(f4s_reduce_argmax_i32, ArgmaxKeyI32, 2, 8)
 F4S_ARGMAX_KERNEL(f4s_reduce_argmax_u32, ArgmaxKeyU32, 2, 8)
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 3, 4)  // f16 and bf16
-F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2, 4)
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 2, 8)  // f16 and bf16
+F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2, 6)    // 8 would spill more
 #undef F4S_ARGMAX_KERNEL
 // the other AccumulatorType inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
 // accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2

@@ -290,8 +290,8 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
 namespace {
 
 // 16-byte vectors per lane per step of each fast kernel (its Op::kUnroll in
-// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums and the i32 / u32 argmax,
-// 4 for the rest.
+// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums and every argmax but
+// f64's (6), 4 for the f32, i32 and u32 sums.
 int reduce_step_vectors(ReduceOp op) {
   switch (op) {
     case ReduceOp::kSumF16:
@@ -299,25 +299,33 @@ int reduce_step_vectors(ReduceOp op) {
     case ReduceOp::kSumF64:
     case ReduceOp::kSumE4m3:
     case ReduceOp::kSumE5m2:
+    case ReduceOp::kArgmaxF32:
     case ReduceOp::kArgmaxI32:
-    case ReduceOp::kArgmaxU32: return kReduceUnroll;
+    case ReduceOp::kArgmaxU32:
+    case ReduceOp::kArgmaxF16:
+    case ReduceOp::kArgmaxBf16: return kReduceUnroll;
+    case ReduceOp::kArgmaxF64: return 6;
     default: return kShortStepUnroll;
   }
 }
 
 // Waves of co-resident clusters in one launch: kReduceWaves, doubled for the
-// kernels that hold two CTAs per SM with 8-vector steps — the f64 and FP8
-// sums and the i32 / u32 argmax (~4544 CTAs either way; measured +2-6 % for
-// the sums and +4 % for the argmax at 2 and 8 GiB over 8 waves of 4-vector
-// steps).  Every choice stays within reduce_workspace_bytes(): at most 4
-// CTAs per SM x kReduceWaves.
+// kernels that hold two CTAs per SM with long steps — the f64 and FP8 sums
+// and every argmax (~4544 CTAs either way; measured +2-6 % for the sums and
+// +0.5-4 % for the argmax at 2 to 16 GiB over 8 waves of 4-vector steps).
+// Every choice stays within reduce_workspace_bytes(): at most 4 CTAs per SM
+// x kReduceWaves.
 int reduce_waves(ReduceOp op) {
   switch (op) {
     case ReduceOp::kSumF64:
     case ReduceOp::kSumE4m3:
     case ReduceOp::kSumE5m2:
+    case ReduceOp::kArgmaxF32:
     case ReduceOp::kArgmaxI32:
-    case ReduceOp::kArgmaxU32: return 2 * kReduceWaves;
+    case ReduceOp::kArgmaxU32:
+    case ReduceOp::kArgmaxF16:
+    case ReduceOp::kArgmaxBf16:
+    case ReduceOp::kArgmaxF64: return 2 * kReduceWaves;
     default: return kReduceWaves;
   }
 }
