@@ -106,9 +106,10 @@ struct SumF64PartialBase {
 };
 
 // f32 in, f64 out: fp32 pairs inside a 16-byte vector, a pairwise fp32
-// tree over the U vectors of a step, f64 above.  The fast kernel steps 4
-// vectors per lane (32 registers, 4 CTAs per SM: +4% at 2^29 elements); the
-// order-fixed kernel's tiles are 8.
+// tree over the U vectors of a step, f64 above.  Both the fast kernel and
+// the order-fixed kernel's tiles step 8 vectors per lane (the fast kernel
+// at 2 CTAs per SM in 16 waves: +1.2 % at 2^32 and +0.4 % at 2^29 elements
+// over 4 vectors at 4 CTAs per SM in 8 waves, A/B on B200).
 template <int U>
 struct SumF32OpT : SumF64PartialBase {
   static constexpr int kElemBytes = 4;
@@ -125,7 +126,7 @@ struct SumF32OpT : SumF64PartialBase {
     t.acc += static_cast<double>(u2f(static_cast<uint32_t>(bits)));
   }
 };
-using SumF32Op = SumF32OpT<4>;         // fast kernel
+using SumF32Op = SumF32OpT<kReduceUnroll>;  // fast kernel
 using SumF32TileOp = SumF32OpT<kReduceUnroll>;  // order-fixed tiles
 
 // 16-bit floats (bf16 or f16) in, f64 out.  Each vector is summed in f32
@@ -216,7 +217,9 @@ using SumF64TileOp = SumF64OpT<kReduceUnroll>;
 // i32 or u32 in, 32-bit two's-complement wrap out (bit-identical for both).
 struct SumWrap32Op {
   static constexpr int kElemBytes = 4;
-  static constexpr int kUnroll = 4;  // 4 vectors per lane per step (+5% at 2^29, +3% at 2^32 over 8)
+  // 8 vectors per lane per step at 2 CTAs per SM in 16 waves: +0.6 % at
+  // 2^32 elements over 4 vectors at 3 CTAs per SM in 8 waves (A/B on B200)
+  static constexpr int kUnroll = kReduceUnroll;
   using Partial = int32_t;
   struct Thread {
     uint32_t acc = 0;
@@ -590,11 +593,8 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
     f4s::reduce_full<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace,                      \
                          f4s::join_u64(base_lo, base_hi), accumulate);                       \
   }
-// f32 -> f64 sum; i32 / u32 -> 32-bit wrapping sum; f32 max/argmax
-F4S_REDUCE_KERNEL(f4s_reduce_sum_f32, f4s::SumF32Op)
-F4S_REDUCE_KERNEL(f4s_reduce_sum_i32, f4s::SumWrap32Op)
-// max / argmax over every OrderedType.  MIN_CTAS: 3 per SM where that
-// fits in registers without spilling (f32, 16-bit), else 2.
+// max / argmax over every OrderedType, 2 CTAs per SM (MIN_CTAS) with
+// UNROLL vectors per lane per step.
 #define F4S_ARGMAX_KERNEL(NAME, KEY, MIN_CTAS, UNROLL)                                                 \
   extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, MIN_CTAS)                             \
       NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace,           \
@@ -613,8 +613,9 @@ F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2, 6)    // 8 would spill
 F4S_REDUCE_KERNEL(f4s_reduce_sum_bf16, f4s::SumHalfOp<true>)
 F4S_REDUCE_KERNEL(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
 #undef F4S_REDUCE_KERNEL
-// f64 and FP8: two CTAs per SM (the register room lets each lane keep two
-// 8-vector steps in flight), launched in twice the waves.
+// f32 -> f64 sum, i32 / u32 -> 32-bit wrapping sum, f64 and FP8: two CTAs
+// per SM (the register room lets each lane keep 8-vector steps in flight),
+// launched in twice the waves.
 #define F4S_REDUCE_KERNEL_2(NAME, OP)                                                        \
   extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, 2)                          \
       NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace, \
@@ -622,6 +623,8 @@ F4S_REDUCE_KERNEL(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
     f4s::reduce_full<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace,                      \
                          f4s::join_u64(base_lo, base_hi), accumulate);                       \
   }
+F4S_REDUCE_KERNEL_2(f4s_reduce_sum_f32, f4s::SumF32Op)
+F4S_REDUCE_KERNEL_2(f4s_reduce_sum_i32, f4s::SumWrap32Op)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_f64, f4s::SumF64Op)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_e4m3, f4s::SumFp8Op<true>)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_e5m2, f4s::SumFp8Op<false>)

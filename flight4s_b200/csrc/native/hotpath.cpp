@@ -17,7 +17,6 @@ namespace {
 // Launch constants shared with the kernels (csrc/kernels/*.cuh).
 constexpr int kReduceBlock = 512;
 constexpr int kReduceUnroll = 8;
-constexpr int kShortStepUnroll = 4;
 constexpr int kReduceWaves = 8;
 constexpr std::uint64_t kReducePartialOffset = 256;
 constexpr std::uint64_t kReducePartialBytes = 16;
@@ -290,43 +289,20 @@ CUresult Hotpath::set_reduce_cluster(int cluster) {
 namespace {
 
 // 16-byte vectors per lane per step of each fast kernel (its Op::kUnroll in
-// reduce.cuh): 8 for the 16-bit, f64 and FP8 sums and every argmax but
-// f64's (6), 4 for the f32, i32 and u32 sums.
-int reduce_step_vectors(ReduceOp op) {
-  switch (op) {
-    case ReduceOp::kSumF16:
-    case ReduceOp::kSumBf16:
-    case ReduceOp::kSumF64:
-    case ReduceOp::kSumE4m3:
-    case ReduceOp::kSumE5m2:
-    case ReduceOp::kArgmaxF32:
-    case ReduceOp::kArgmaxI32:
-    case ReduceOp::kArgmaxU32:
-    case ReduceOp::kArgmaxF16:
-    case ReduceOp::kArgmaxBf16: return kReduceUnroll;
-    case ReduceOp::kArgmaxF64: return 6;
-    default: return kShortStepUnroll;
-  }
-}
+// reduce.cuh): 8, except 6 for the f64 argmax.
+int reduce_step_vectors(ReduceOp op) { return op == ReduceOp::kArgmaxF64 ? 6 : kReduceUnroll; }
 
-// Waves of co-resident clusters in one launch: kReduceWaves, doubled for the
-// kernels that hold two CTAs per SM with long steps — the f64 and FP8 sums
-// and every argmax (~4544 CTAs either way; measured +2-6 % for the sums and
-// +0.5-4 % for the argmax at 2 to 16 GiB over 8 waves of 4-vector steps).
-// Every choice stays within reduce_workspace_bytes(): at most 4 CTAs per SM
-// x kReduceWaves.
+// Waves of co-resident clusters in one launch: twice kReduceWaves for the
+// kernels that hold two CTAs per SM (every sum but the 16-bit ones, every
+// argmax: ~4544 CTAs; measured +0.5-6 % over 8 waves of 4-vector steps at
+// 2 to 16 GiB), kReduceWaves for the 16-bit sums (3 CTAs per SM).  Every
+// choice stays within reduce_workspace_bytes(): at most 4 CTAs per SM x
+// kReduceWaves.
 int reduce_waves(ReduceOp op) {
   switch (op) {
-    case ReduceOp::kSumF64:
-    case ReduceOp::kSumE4m3:
-    case ReduceOp::kSumE5m2:
-    case ReduceOp::kArgmaxF32:
-    case ReduceOp::kArgmaxI32:
-    case ReduceOp::kArgmaxU32:
-    case ReduceOp::kArgmaxF16:
-    case ReduceOp::kArgmaxBf16:
-    case ReduceOp::kArgmaxF64: return 2 * kReduceWaves;
-    default: return kReduceWaves;
+    case ReduceOp::kSumF16:
+    case ReduceOp::kSumBf16: return kReduceWaves;
+    default: return 2 * kReduceWaves;
   }
 }
 

@@ -171,7 +171,7 @@ def hotpath_dispatch():
     check("f4s_fp8_quant_rows", hp_fp8_rows_grid())
     out = ctx.allocate("i64", 2)
     hp.reduce_into(f4s.REDUCE_SUM_F32, big, out, n=1 << 32)
-    L = check("f4s_reduce_sum_f32", 37 * 8 * 4, block=512, cluster=4)
+    L = check("f4s_reduce_sum_f32", 37 * 16 * 4, block=512, cluster=4)  # 16 waves of the fake's 37 clusters
     assert (param(L, 1, 4), param(L, 2, 4)) == (0, 1)  # n = 2^32 split in two u32
     assert L.programmatic == 0  # launch overlap is off by default
     hp.reduce_into(f4s.REDUCE_ARGMAX_F32, big, out, n=1000, index_base=(1 << 32) + 5, accumulate=True)
@@ -180,7 +180,8 @@ def hotpath_dispatch():
     # with launch overlap the device-resident reductions are programmatic dependents
     hp.set_launch_overlap(True)
     hp.reduce_into(f4s.REDUCE_SUM_I32, big, out, n=1 << 20)
-    assert check("f4s_reduce_sum_i32", 32 * 4, block=512, cluster=4).programmatic == 1
+    # 8 vectors per lane per step: 16 clusters of 4 x 512 x 4 x 8 elements
+    assert check("f4s_reduce_sum_i32", 16 * 4, block=512, cluster=4).programmatic == 1
     hp.reduce_sum_into("bf16", big, out, n=1000)
     assert last().programmatic == 1
     hp.vector_add_f32(big, big, big, n=1 << 10)  # other operators never are
@@ -227,7 +228,7 @@ def hotpath_dispatch():
     assert (param(L, 1, 4), param(L, 6, 4)) == (1 << 20, 0)
     assert param(L, 5, 8) - param(L, 4, 8) == 256      # group partials follow the 256-byte ticket
     hp.reduce_sum_into("i32", big, out, n=1 << 20, policy="strict")   # integers: exact under any policy
-    check("f4s_reduce_sum_i32", 32 * 4, block=512, cluster=4)
+    check("f4s_reduce_sum_i32", 16 * 4, block=512, cluster=4)
     hp.reduce_ordered_final_into(wso.address + 256, 16, out, accumulate=True)
     L = check("f4s_reduce_ordered_final", 1, block=512)
     assert (param(L, 1, 4), param(L, 4, 4)) == (16, 1)
