@@ -586,13 +586,6 @@ __device__ __forceinline__ void reduce_full(const void* __restrict__ in_ptr, uin
 // Kernel entry points.  Parameters use only launch-ABI descriptor codes
 // 10 (device pointer), 3 (u32) and 2 (i32): (in, n_lo, n_hi, out, workspace,
 // index_base_lo, index_base_hi, accumulate).
-#define F4S_REDUCE_KERNEL(NAME, OP)                                                          \
-  extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock)                             \
-      NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace, \
-           uint32_t base_lo, uint32_t base_hi, int accumulate) {                              \
-    f4s::reduce_full<OP>(in, f4s::join_u64(n_lo, n_hi), out, workspace,                      \
-                         f4s::join_u64(base_lo, base_hi), accumulate);                       \
-  }
 // max / argmax over every OrderedType, 2 CTAs per SM (MIN_CTAS) with
 // UNROLL vectors per lane per step.
 #define F4S_ARGMAX_KERNEL(NAME, KEY, MIN_CTAS, UNROLL)                                                 \
@@ -608,14 +601,12 @@ F4S_ARGMAX_KERNEL(f4s_reduce_argmax_u32, ArgmaxKeyU32, 2, 8)
 F4S_ARGMAX_KERNEL(f4s_reduce_argmax_half, ArgmaxKeyHalf, 2, 8)  // f16 and bf16
 F4S_ARGMAX_KERNEL(f4s_reduce_argmax_f64, ArgmaxKeyF64, 2, 6)    // 8 would spill more
 #undef F4S_ARGMAX_KERNEL
-// the other AccumulatorType inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
-// accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2
-F4S_REDUCE_KERNEL(f4s_reduce_sum_bf16, f4s::SumHalfOp<true>)
-F4S_REDUCE_KERNEL(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
-#undef F4S_REDUCE_KERNEL
-// f32 -> f64 sum, i32 / u32 -> 32-bit wrapping sum, f64 and FP8: two CTAs
-// per SM (the register room lets each lane keep 8-vector steps in flight),
-// launched in twice the waves.
+// Sums: f32 -> f64, i32 / u32 -> 32-bit wrap, and the other AccumulatorType
+// inputs (core/src/main/scala/flight4s/core/types/CudaType.scala:199-230),
+// accumulated in f64: bf16, f16, f64, FP8 E4M3, FP8 E5M2.  Two CTAs per SM
+// (the register room lets each lane keep 8-vector steps in flight),
+// launched in twice the waves; for bf16 / f16 +1.0 % at 8 GiB and +1.2 % at
+// 2 GiB over 3 CTAs per SM in 8 waves (A/B on B200).
 #define F4S_REDUCE_KERNEL_2(NAME, OP)                                                        \
   extern "C" __global__ void __launch_bounds__(f4s::kReduceBlock, 2)                          \
       NAME(const void* in, uint32_t n_lo, uint32_t n_hi, void* out, unsigned char* workspace, \
@@ -626,6 +617,8 @@ F4S_REDUCE_KERNEL(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_f32, f4s::SumF32Op)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_i32, f4s::SumWrap32Op)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_f64, f4s::SumF64Op)
+F4S_REDUCE_KERNEL_2(f4s_reduce_sum_bf16, f4s::SumHalfOp<true>)
+F4S_REDUCE_KERNEL_2(f4s_reduce_sum_f16, f4s::SumHalfOp<false>)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_e4m3, f4s::SumFp8Op<true>)
 F4S_REDUCE_KERNEL_2(f4s_reduce_sum_e5m2, f4s::SumFp8Op<false>)
 #undef F4S_REDUCE_KERNEL_2

@@ -292,19 +292,12 @@ namespace {
 // reduce.cuh): 8, except 6 for the f64 argmax.
 int reduce_step_vectors(ReduceOp op) { return op == ReduceOp::kArgmaxF64 ? 6 : kReduceUnroll; }
 
-// Waves of co-resident clusters in one launch: twice kReduceWaves for the
-// kernels that hold two CTAs per SM (every sum but the 16-bit ones, every
-// argmax: ~4544 CTAs; measured +0.5-6 % over 8 waves of 4-vector steps at
-// 2 to 16 GiB), kReduceWaves for the 16-bit sums (3 CTAs per SM).  Every
-// choice stays within reduce_workspace_bytes(): at most 4 CTAs per SM x
+// Waves of co-resident clusters in one launch: every fast kernel holds two
+// CTAs per SM, launched in twice kReduceWaves (~4544 CTAs; measured +0.5-6 %
+// over 8 waves of 4-vector steps or 3-4 CTAs per SM at 2 to 16 GiB).  This
+// stays within reduce_workspace_bytes(): at most 4 CTAs per SM x
 // kReduceWaves.
-int reduce_waves(ReduceOp op) {
-  switch (op) {
-    case ReduceOp::kSumF16:
-    case ReduceOp::kSumBf16: return kReduceWaves;
-    default: return 2 * kReduceWaves;
-  }
-}
+int reduce_waves(ReduceOp) { return 2 * kReduceWaves; }
 
 }  // namespace
 

@@ -206,7 +206,7 @@ def hotpath_dispatch():
     hp.reduce_sum_into("e5m2", big, out, n=1 << 30)
     check("f4s_reduce_sum_e5m2", 37 * 16 * 4, block=512, cluster=4)
     hp.reduce_sum_into("f16", big, out, n=1 << 29)
-    check("f4s_reduce_sum_f16", 37 * 8 * 4, block=512, cluster=4)
+    check("f4s_reduce_sum_f16", 37 * 16 * 4, block=512, cluster=4)
     assert 256 + 16 * (37 * 16) <= hp.workspace_bytes   # one 16-byte partial slot per launched cluster
     before = count()
     ws0 = hp.workspace()
