@@ -293,11 +293,11 @@ namespace {
 int reduce_step_vectors(ReduceOp op) { return op == ReduceOp::kArgmaxF64 ? 6 : kReduceUnroll; }
 
 // Waves of co-resident clusters in one launch: every fast kernel holds two
-// CTAs per SM, launched in twice kReduceWaves (~4544 CTAs; measured +0.5-6 %
-// over 8 waves of 4-vector steps or 3-4 CTAs per SM at 2 to 16 GiB).  This
-// stays within reduce_workspace_bytes(): at most 4 CTAs per SM x
-// kReduceWaves.
-int reduce_waves(ReduceOp) { return 2 * kReduceWaves; }
+// CTAs per SM and is launched in twice kReduceWaves waves (~4544 CTAs;
+// measured +0.5-6 % over 8 waves of 4-vector steps at 3-4 CTAs per SM, 2 to
+// 16 GiB).  This stays within reduce_workspace_bytes(): at most 4 CTAs per
+// SM x kReduceWaves.
+constexpr int kReduceLaunchWaves = 2 * kReduceWaves;
 
 }  // namespace
 
@@ -339,14 +339,14 @@ CUresult Hotpath::reduce_launch(ReduceOp op, CUstream stream, CUdeviceptr in, st
   if (workspace % 16 != 0) throw std::invalid_argument("reduction workspace must be 16-byte aligned");
   const int cluster = shape_.reduce_cluster;
   // Enough clusters to give each thread >= one unrolled step of 16-byte
-  // vectors, at most kReduceWaves waves of co-resident clusters (several
-  // waves measured faster than one persistent wave: no idle tail).
+  // vectors, at most kReduceLaunchWaves waves of co-resident clusters
+  // (several waves measured faster than one persistent wave: no idle tail).
   const std::uint64_t per_cluster =
       static_cast<std::uint64_t>(cluster) * kReduceBlock * (16 / elem) * reduce_step_vectors(op);
   const std::uint64_t wanted = std::max<std::uint64_t>(1, (n + per_cluster - 1) / per_cluster);
   const int clusters = static_cast<int>(
       std::min<std::uint64_t>(wanted, static_cast<std::uint64_t>(shape_.reduce_max_clusters[static_cast<int>(op)]) *
-                                          reduce_waves(op)));
+                                          kReduceLaunchWaves));
   const std::uint64_t need = kReducePartialOffset + kReducePartialBytes * static_cast<std::uint64_t>(clusters);
   if (workspace_bytes < need) {
     throw std::invalid_argument("reduction workspace too small: " + std::to_string(workspace_bytes) +
